@@ -1,0 +1,180 @@
+/*
+ * tokengate_b200 — C ABI of the B200 (sm_100a) gated-prefill kernels.
+ *
+ * Plain pointers, sizes and strides; no framework types. Every entry point:
+ *   - returns TG_OK (0) or a tg_status code; tg_last_error() gives a message
+ *     for the calling thread's most recent failure;
+ *   - is asynchronous on `stream` (a cudaStream_t passed as void*; NULL is the
+ *     legacy default stream) and allocates no device memory: the caller owns
+ *     every buffer;
+ *   - runs on the device that is current on the calling thread, which must be
+ *     the device holding the buffers.
+ * Kernels whose internal waits give up (see tg_device_error) record a flag on
+ * the device instead of hanging; the host can read it after synchronising.
+ *
+ * Strides are in ELEMENTS unless the name says bytes.
+ */
+#ifndef TOKENGATE_B200_H
+#define TOKENGATE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TG_ABI_VERSION 1
+
+typedef enum {
+  TG_OK = 0,
+  TG_ERR_INVALID_ARGUMENT = 1, /* a shape, count or pointer is invalid   */
+  TG_ERR_UNSUPPORTED = 2,      /* valid, but not served (e.g. head_dim)  */
+  TG_ERR_ALIGNMENT = 3,        /* a pointer or stride breaks alignment   */
+  TG_ERR_CUDA = 4              /* a CUDA runtime/driver call failed      */
+} tg_status;
+
+/* ABI stamp (TG_ABI_VERSION of the built library). Mirrors the loader's ABI
+ * check of the reference extension (kernels/fa2bias/site_path.py:6-8,
+ * kernels/fa2bias/keybias.py:29-37). */
+int tg_abi_version(void);
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* tg_last_error(void);
+
+/* Reads the device-side error word of the current device (bit flags set by a
+ * kernel whose bounded wait timed out; 0 = none). Synchronises `stream`.
+ * clear != 0 resets the word to 0 afterwards. */
+int tg_device_error(void* stream, unsigned int* flags_out, int clear);
+
+/*
+ * a1 — causal GQA attention with an additive per-key bias, forward.
+ *
+ * Replaces the reference key-bias operator
+ *   torch.ops.recursive_kvs.fa2_keybias_fwd(q, k, v, bias_raw, scale, causal)
+ *   (kernels/fa2bias/keybias.py:40-45; wrapper flash_attn_key_bias :85-87;
+ *    kernel kernels/fa2bias/keybias.patch:276-461)
+ * and the FlexAttention key-bias score_mod path
+ *   (tokengate/e2e_gate/attn/flex_attention_utils.py:174-198, :233-287).
+ *
+ *   out[b,i,h,:] = sum_j softmax_j( softmax_scale * qs[b,h,i] * q[b,i,h,:].k[b,j,g,:]
+ *                                   + bias[b,h,j] ) * v[b,j,g,:],   g = h / (Hq/Hkv)
+ *   j <= i when causal (then Sq must equal Sk).
+ *   lse[b,h,i] = log sum_j exp(...)  (natural log, fp32)
+ *
+ * The bias is in score units (what the flex score_mod adds), i.e. the
+ * reference's bias_raw * softmax_scale. bias_sh == 0 broadcasts one row over
+ * all heads (the reference's scalar (S,)/(B,S) layouts); bias_sb == 0
+ * broadcasts over the batch. Finite large negative values (the reference pads
+ * with -1e9) are treated as ordinary finite biases.
+ *
+ * q: (B, Sq, Hq, D) bf16 with strides (q_sb, q_ss, q_sh, 1); k, v likewise
+ * with Sk, Hkv. Only D == 128 is served. Bases 16-byte aligned and the batch,
+ * row and head strides multiples of 8 elements (TMA).
+ * bias: fp32, (B, Hq, Sk) with strides (bias_sb, bias_sh, 1), nullable.
+ * q_row_scale: fp32, (B, Hq, Sq) with strides (qs_sb, qs_sh, 1), nullable:
+ *   the per-row query scale of the Phase-2 prologue
+ *   (tokengate/e2e_gate/attn/qwen3_flex_attention.py:433-473).
+ * out: bf16 (B, Sq, Hq, D) strides (o_sb, o_ss, o_sh, 1).
+ * lse: fp32 (B, Hq, Sq) strides (lse_sb, lse_sh, 1), nullable.
+ */
+int tg_keybias_attn_fwd(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
+                        const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                        const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                        const float* bias, int64_t bias_sb, int64_t bias_sh,
+                        const float* q_row_scale, int64_t qs_sb, int64_t qs_sh,
+                        void* out, int64_t o_sb, int64_t o_ss, int64_t o_sh,
+                        float* lse, int64_t lse_sb, int64_t lse_sh,
+                        int B, int Sq, int Sk, int Hq, int Hkv, int D,
+                        float softmax_scale, int causal, void* stream);
+
+/*
+ * a4 — gate scorer: score[b, r] = logsigmoid( sum_e float(h[b, row_begin[b]+r, e]) * w[e] )
+ * for r < row_count[b].
+ *
+ * Replaces the synthetic linear gate's scoring of the state span,
+ *   b_scores = gate(h_art.to(fp32))  with a fp32 1-wide readout + logsigmoid
+ *   (tokengate/e2e_gate/gate_module/gate_forward.py:1396-1407; fixture shape
+ *    of tests/inference/test_prefill_memory.py:18-33).
+ * The dot product has a fixed summation order and logsigmoid is computed
+ * with IEEE operations only, so results are reproducible bit for bit.
+ *
+ * hidden: bf16 (B, S, hidden_dim), strides (h_sb, h_ss, 1); hidden_dim one of
+ * 256, 512, 1024, 2048, 2560, 4096, 5120; rows 16-byte aligned.
+ * w: fp32 (hidden_dim,). row_begin / row_count: HOST arrays of B ints.
+ * scores: fp32 (B, >= max row_count), batch stride s_sb.
+ */
+int tg_gate_score(const void* hidden, int64_t h_sb, int64_t h_ss, int hidden_dim,
+                  const float* w, int B, const int32_t* row_begin, const int32_t* row_count,
+                  float* scores, int64_t s_sb, void* stream);
+
+/*
+ * a6 + a7 (positions, bias) — top-K selection and the kept-position list.
+ *
+ * Replaces, per request b, the selection and keep-list construction
+ *   K_clamped = max(1, min(K, n_art)); topk = torch.topk(score, K_clamped)
+ *   keep = [0, start) ++ start + sort(topk) ++ [end, seq_len)
+ *   (tokengate/e2e_gate/gate_module/gate_forward.py:84-99, :1409-1421)
+ * and the Phase-2 bias row and padding
+ *   gate_bias[b, :n_kept] = score at kept state tokens, 0 elsewhere;
+ *   gate_bias[b, n_kept:] = -1e9   (:968-1036, :1463-1469).
+ * Ordering contract: by (score descending, index ascending), so ties at the
+ * K-th value keep the lower indices. Scores are compared as IEEE floats
+ * (-0.0 < +0.0; NaNs are not supported).
+ *
+ * scores: fp32 (B, >= n_state[b]), batch stride s_sb.
+ * n_state, k, state_begin, seq_len: HOST arrays of B ints; k is K_clamped
+ * (1 <= k <= n_state). n_kept[b] = state_begin + k + (seq_len - state_begin - n_state)
+ * must be <= n_alloc.
+ * keep: int64 (B, n_alloc), batch stride keep_sb: kept ORIGINAL positions in
+ *   ascending order, slots >= n_kept set to 0.
+ * bias_out (nullable): (B, n_alloc) in bias_dtype (0 = fp32, 1 = bf16),
+ *   batch stride bias_sb.
+ * topk_local (nullable): int64 (B, >= k), batch stride tl_sb: the selected
+ *   state-relative indices in ascending order.
+ */
+int tg_topk_select(const float* scores, int64_t s_sb, int B, const int32_t* n_state,
+                   const int32_t* k, const int32_t* state_begin, const int32_t* seq_len,
+                   int n_alloc, int64_t* keep, int64_t keep_sb, void* bias_out, int64_t bias_sb,
+                   int bias_dtype, int64_t* topk_local, int64_t tl_sb, void* stream);
+
+/*
+ * a7 / a8 — compaction: gather kept rows of several tensors in one launch.
+ *
+ * Replaces hs_pruned[b, :n] = hidden_states[b, keep]
+ *   (tokengate/e2e_gate/gate_module/gate_forward.py:1443-1461)
+ * and the below-gate K/V gathers of prefill_batch_for_decode
+ *   (index_select + pad, :1491-1522; B=1 form prune_kv_cache :1078-1097).
+ *
+ * For each tensor t, request b < B and row r < n_rows:
+ *   r <  n_valid[b]: dst row r <- src row idx[b, r]
+ *   r >= n_valid[b]: dst row r <- zeros
+ * A row is n_seg segments of seg_bytes at seg_stride (one segment for a
+ * (B, S, ...) token-major tensor, one per head for a (B, H, S, D) one).
+ * Addresses, strides and seg_bytes must be multiples of 16 bytes.
+ * idx: int64 device array (B, >= n_rows), batch stride idx_sb; every index
+ * used must be in range for the source (the caller's contract).
+ * n_valid: HOST array of B ints. At most TG_MAX_GATHER_TENSORS tensors.
+ */
+#define TG_MAX_GATHER_TENSORS 16
+typedef struct {
+  const void* src;
+  void* dst;
+  int64_t src_batch_stride; /* bytes */
+  int64_t src_row_stride;   /* bytes */
+  int64_t src_seg_stride;   /* bytes */
+  int64_t dst_batch_stride; /* bytes */
+  int64_t dst_row_stride;   /* bytes */
+  int64_t dst_seg_stride;   /* bytes */
+  int64_t seg_bytes;
+  int32_t n_seg;
+  int32_t reserved;
+} tg_gather_tensor;
+
+int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t* idx,
+                   int64_t idx_sb, int B, int n_rows, const int32_t* n_valid, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TOKENGATE_B200_H */

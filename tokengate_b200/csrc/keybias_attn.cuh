@@ -1,0 +1,469 @@
+// Causal GQA attention with an additive per-key bias — sm_100a forward kernel.
+//
+// Semantics follow the reference key-bias operator (softmax(scale*q.k + b)v,
+// kernels/fa2bias/keybias.patch:387-461 and the FlexAttention score_mod
+// tokengate/e2e_gate/attn/flex_attention_utils.py:174-198); the design is
+// Blackwell-native:
+//
+//  * one CTA owns TWO 128-row query tiles that share one KV head: two heads
+//    of a GQA group at the same rows (Hq/Hkv even), or two consecutive row
+//    blocks of one head otherwise. K/V tiles are loaded once for both.
+//  * warp 8 streams Q/K/V through TMA (128-byte swizzle, no multicast) into a
+//    2-stage ring and stages the bias of each key block (pre-multiplied by
+//    log2 e, -inf past Sk) next to the V tile;
+//  * warp 9 issues tcgen05.mma (M=128, N=128, K=16 steps): S_t = Q_t K^T into
+//    TMEM, then O_t += P_t V with P read straight from TMEM (it overwrites
+//    the first 64 columns of S_t as packed bf16 pairs);
+//  * warps 0-3 / 4-7 are the softmax warpgroups of tile 0 / tile 1: one TMEM
+//    lane (= one query row) per thread, the whole 128-key row in registers,
+//    x = S*scale*log2e + bias*log2e in one FFMA, exp2 on the MUFU. The running
+//    max is only moved (and O rescaled in TMEM) when it grows by more than
+//    2^8, so rescales are rare; numerator and denominator share the stale max,
+//    so the result is exact.
+//  * TMEM: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512) columns.
+//
+// Issue order of the MMA warp per key block j (tile 0, tile 1):
+//   O0 += P0_j V_j ; S0 = Q0 K_{j+1} ; O1 += P1_j V_j ; S1 = Q1 K_{j+1}
+// so each softmax warpgroup works while the tensor core runs the other
+// tile's two MMAs. The tensor pipe executes one thread's MMAs in issue order,
+// which is what makes writing S_t after the P_t V read safe.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace tg {
+
+constexpr int kAttnBM = 128;
+constexpr int kAttnBN = 128;
+constexpr int kAttnD = 128;
+constexpr int kAttnThreads = 320;
+constexpr int kAttnTileBytes = kAttnBM * kAttnD * 2;  // 32 KB: one Q/K/V tile
+constexpr int kAttnHalfBytes = kAttnTileBytes / 2;    // 16 KB: 64 columns (one TMA box)
+
+// dynamic shared memory layout (offsets from a 1024-byte aligned base)
+constexpr int kSmQ = 0;                                  // 2 tiles
+constexpr int kSmK = kSmQ + 2 * kAttnTileBytes;          // 2 stages
+constexpr int kSmV = kSmK + 2 * kAttnTileBytes;          // 2 stages
+constexpr int kSmBias = kSmV + 2 * kAttnTileBytes;       // [stage][tile][128] fp32
+constexpr int kSmBar = kSmBias + 2 * 2 * kAttnBN * 4;
+constexpr int kNumBars = 16;
+constexpr int kSmTmemSlot = kSmBar + kNumBars * 8;
+constexpr int kAttnSmemBytes = kSmTmemSlot + 16 + 1024;  // + alignment slack
+
+// barrier indices
+enum {
+  BAR_Q = 0,
+  BAR_K_FULL = 1,   // 2
+  BAR_K_EMPTY = 3,  // 2
+  BAR_V_FULL = 5,   // 2
+  BAR_V_EMPTY = 7,  // 2
+  BAR_S_FULL = 9,   // 2 (per tile)
+  BAR_P_FULL = 11,  // 2 (per tile)
+  BAR_O_FULL = 13,  // 2 (per tile)
+  BAR_MMA_DONE = 15
+};
+
+// device error bits
+enum : unsigned int {
+  ERR_ATTN_Q = 1u << 0,
+  ERR_ATTN_K_EMPTY = 1u << 1,
+  ERR_ATTN_V_EMPTY = 1u << 2,
+  ERR_ATTN_K_FULL = 1u << 3,
+  ERR_ATTN_V_FULL = 1u << 4,
+  ERR_ATTN_P_FULL = 1u << 5,
+  ERR_ATTN_S_FULL = 1u << 6,
+  ERR_ATTN_O_FULL = 1u << 7,
+  ERR_ATTN_DRAIN = 1u << 8,
+};
+
+struct AttnParams {
+  const float* bias;
+  int64_t bias_sb, bias_sh;
+  const float* qscale;
+  int64_t qs_sb, qs_sh;
+  __nv_bfloat16* out;
+  int64_t o_sb, o_ss, o_sh;
+  float* lse;
+  int64_t lse_sb, lse_sh;
+  int B, Sq, Sk, Hq, Hkv, G;
+  int pair_heads;  // 1: tiles are heads (2p, 2p+1) at one row block
+  int causal;
+  int n_mblocks;   // ceil(Sq / 128)
+  int n_kblocks;   // ceil(Sk / 128)
+  int heads_per_unit_row;  // pair_heads ? Hq/2 : Hq
+  float scale_log2;        // softmax_scale * log2(e)
+  unsigned int* err;
+};
+
+struct TileInfo {
+  int head;
+  int m0;
+  int nblk;  // key blocks this tile needs (0 = tile unused)
+};
+
+__device__ __forceinline__ void attn_unit(const AttnParams& p, TileInfo (&ti)[2]) {
+  const int u = blockIdx.x;
+  if (p.pair_heads) {
+    const int hp = u % p.heads_per_unit_row;
+    const int mb = p.n_mblocks - 1 - u / p.heads_per_unit_row;  // heavy rows first
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      ti[t].head = 2 * hp + t;
+      ti[t].m0 = mb * kAttnBM;
+    }
+  } else {
+    const int h = u % p.heads_per_unit_row;
+    const int n_pairs = (p.n_mblocks + 1) / 2;
+    const int pr = n_pairs - 1 - u / p.heads_per_unit_row;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      ti[t].head = h;
+      ti[t].m0 = (2 * pr + t) * kAttnBM;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    if (ti[t].m0 >= p.Sq) {
+      ti[t].nblk = 0;
+    } else if (p.causal) {
+      ti[t].nblk = min(p.n_kblocks, ti[t].m0 / kAttnBN + 1);
+    } else {
+      ti[t].nblk = p.n_kblocks;
+    }
+  }
+}
+
+// all lanes wait; the result is made warp-uniform
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, unsigned int* err,
+                                          unsigned int code) {
+  const bool ok = mbar_wait(bar, parity, err, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    keybias_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
+                            const __grid_constant__ CUtensorMap tm_k,
+                            const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sQ = sbase + kSmQ, sK = sbase + kSmK, sV = sbase + kSmV;
+  float* sBias = reinterpret_cast<float*>(smem + kSmBias);
+  const uint32_t sBar = sbase + kSmBar;
+  auto bar = [&](int i) { return sBar + 8u * i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmTmemSlot);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+
+  TileInfo ti[2];
+  attn_unit(p, ti);
+  const int kvh = ti[0].head / p.G;
+  const int nblk = max(ti[0].nblk, ti[1].nblk);
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(BAR_Q), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(BAR_K_FULL + s), 1);
+      mbar_init(bar(BAR_K_EMPTY + s), 1);
+      mbar_init(bar(BAR_V_FULL + s), 1);
+      mbar_init(bar(BAR_V_EMPTY + s), 1);
+      mbar_init(bar(BAR_S_FULL + s), 1);
+      mbar_init(bar(BAR_P_FULL + s), 4);
+      mbar_init(bar(BAR_O_FULL + s), 1);
+    }
+    mbar_init(bar(BAR_MMA_DONE), 1);
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      const int nq = (ti[0].nblk > 0) + (ti[1].nblk > 0);
+      mbar_arrive_expect_tx(bar(BAR_Q), nq * kAttnTileBytes);
+      for (int t = 0; t < 2; ++t) {
+        if (ti[t].nblk == 0) continue;
+        const uint32_t dst = sQ + t * kAttnTileBytes;
+        tma_load_4d(dst, &tm_q, bar(BAR_Q), 0, ti[t].head, ti[t].m0, b);
+        tma_load_4d(dst + kAttnHalfBytes, &tm_q, bar(BAR_Q), 64, ti[t].head, ti[t].m0, b);
+      }
+    }
+    const float kLog2e = 1.4426950408889634f;
+    int issued = 0;
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (!warp_wait(bar(BAR_K_EMPTY + s), ph ^ 1, p.err, ERR_ATTN_K_EMPTY)) break;
+      if (lane == 0) {
+        const uint32_t dst = sK + s * kAttnTileBytes;
+        mbar_arrive_expect_tx(bar(BAR_K_FULL + s), kAttnTileBytes);
+        tma_load_4d(dst, &tm_k, bar(BAR_K_FULL + s), 0, kvh, j * kAttnBN, b);
+        tma_load_4d(dst + kAttnHalfBytes, &tm_k, bar(BAR_K_FULL + s), 64, kvh, j * kAttnBN, b);
+      }
+      if (!warp_wait(bar(BAR_V_EMPTY + s), ph ^ 1, p.err, ERR_ATTN_V_EMPTY)) {
+        issued = 2 * j + 1;
+        break;
+      }
+      // bias of key block j for both tiles, in log2 units; -inf past Sk
+      float* bdst = sBias + s * 2 * kAttnBN;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i;
+        const int t = e >> 7, c = e & 127;
+        const int key = j * kAttnBN + c;
+        float val;
+        if (key >= p.Sk) {
+          val = -INFINITY;
+        } else if (p.bias != nullptr) {
+          const int hh = t ? ti[1].head : ti[0].head;
+          val = __ldg(p.bias + (int64_t)b * p.bias_sb + (int64_t)hh * p.bias_sh + key) * kLog2e;
+        } else {
+          val = 0.f;
+        }
+        bdst[e] = val;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t dst = sV + s * kAttnTileBytes;
+        mbar_arrive_expect_tx(bar(BAR_V_FULL + s), kAttnTileBytes);
+        tma_load_4d(dst, &tm_v, bar(BAR_V_FULL + s), 0, kvh, j * kAttnBN, b);
+        tma_load_4d(dst + kAttnHalfBytes, &tm_v, bar(BAR_V_FULL + s), 64, kvh, j * kAttnBN, b);
+      }
+      issued = 2 * j + 2;
+    }
+    // drain: make sure no TMA write is still in flight when the CTA retires
+    // (only matters when a wait above gave up).
+    {
+      const int nk = (issued + 1) / 2;  // K loads issued
+      const int nv = issued / 2;        // V loads issued
+      for (int s = 0; s < 2; ++s) {
+        // last use of stage s among the issued loads
+        const int lastk = (nk - 1 - s) >= 0 ? ((nk - 1 - s) & ~1) + s : -1;
+        const int lastv = (nv - 1 - s) >= 0 ? ((nv - 1 - s) & ~1) + s : -1;
+        if (lastk >= 0) mbar_wait(bar(BAR_K_FULL + s), (lastk >> 1) & 1, p.err, ERR_ATTN_DRAIN);
+        if (lastv >= 0) mbar_wait(bar(BAR_V_FULL + s), (lastv >> 1) & 1, p.err, ERR_ATTN_DRAIN);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescQK = umma_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t kIdescPV = umma_idesc_bf16(128, 128, 0, 1);
+      auto issue_qk = [&](int t, int s) {
+        const uint32_t qa = sQ + t * kAttnTileBytes, ka = sK + s * kAttnTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kAttnHalfBytes + (kk & 3) * 32;
+          umma_ss(tmem + t * 128u, umma_desc_sw128(qa + off, 16, 1024),
+                  umma_desc_sw128(ka + off, 16, 1024),
+                  kIdescQK, kk > 0);
+        }
+      };
+      auto issue_pv = [&](int t, int s, bool acc) {
+        const uint32_t va = sV + s * kAttnTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          umma_ts(tmem + 256u + t * 128u, tmem + t * 128u + kk * 8,
+                  umma_desc_sw128(va + kk * 2048, kAttnHalfBytes, 1024),
+                  kIdescPV, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(bar(BAR_Q), 0, p.err, ERR_ATTN_Q);
+      if (ok && nblk > 0) ok = mbar_wait(bar(BAR_K_FULL + 0), 0, p.err, ERR_ATTN_K_FULL);
+      if (ok && nblk > 0) {
+        tc_fence_after();
+        for (int t = 0; t < 2; ++t) {
+          if (ti[t].nblk > 0) {
+            issue_qk(t, 0);
+            umma_commit(bar(BAR_S_FULL + t));
+          }
+        }
+        umma_commit(bar(BAR_K_EMPTY + 0));
+      }
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int s = j & 1;
+        const int s1 = (j + 1) & 1;
+        const bool more = (j + 1) < nblk;
+        if (!mbar_wait(bar(BAR_V_FULL + s), (j >> 1) & 1, p.err, ERR_ATTN_V_FULL)) break;
+        if (j < ti[0].nblk) {
+          if (!mbar_wait(bar(BAR_P_FULL + 0), j & 1, p.err, ERR_ATTN_P_FULL)) break;
+          tc_fence_after();
+          issue_pv(0, s, j > 0);
+          if (j == ti[0].nblk - 1) umma_commit(bar(BAR_O_FULL + 0));
+        }
+        if (more) {
+          if (!mbar_wait(bar(BAR_K_FULL + s1), ((j + 1) >> 1) & 1, p.err, ERR_ATTN_K_FULL)) break;
+          tc_fence_after();
+          if (j + 1 < ti[0].nblk) {
+            issue_qk(0, s1);
+            umma_commit(bar(BAR_S_FULL + 0));
+          }
+        }
+        if (j < ti[1].nblk) {
+          if (!mbar_wait(bar(BAR_P_FULL + 1), j & 1, p.err, ERR_ATTN_P_FULL)) break;
+          tc_fence_after();
+          issue_pv(1, s, j > 0);
+          if (j == ti[1].nblk - 1) umma_commit(bar(BAR_O_FULL + 1));
+        }
+        umma_commit(bar(BAR_V_EMPTY + s));
+        if (more) {
+          if (j + 1 < ti[1].nblk) {
+            issue_qk(1, s1);
+            umma_commit(bar(BAR_S_FULL + 1));
+          }
+          umma_commit(bar(BAR_K_EMPTY + s1));
+        }
+      }
+      // every MMA issued so far has completed before TMEM is released
+      umma_commit(bar(BAR_MMA_DONE));
+      mbar_wait(bar(BAR_MMA_DONE), 0, p.err, ERR_ATTN_DRAIN);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t = warp >> 2;
+    const int sub = warp & 3;
+    const int r = sub * 32 + lane;  // row inside the tile == TMEM lane
+    const TileInfo me = t ? ti[1] : ti[0];
+    const int i = me.m0 + r;        // query index
+    const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
+    const uint32_t tS = tmem + t * 128u + lane_off;
+    const uint32_t tO = tmem + 256u + t * 128u + lane_off;
+
+    float rowscale = p.scale_log2;
+    if (p.qscale != nullptr && i < p.Sq)
+      rowscale *= __ldg(p.qscale + (int64_t)b * p.qs_sb + (int64_t)me.head * p.qs_sh + i);
+
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    const int diag_blk = p.causal ? (me.m0 / kAttnBN) : -1;
+
+    for (int j = 0; j < me.nblk; ++j) {
+      const int s = j & 1;
+      if (!warp_wait(bar(BAR_S_FULL + t), j & 1, p.err, ERR_ATTN_S_FULL)) { ok = false; break; }
+      if (!warp_wait(bar(BAR_V_FULL + s), (j >> 1) & 1, p.err, ERR_ATTN_V_FULL)) { ok = false; break; }
+      tc_fence_after();
+
+      uint32_t sv[128];
+      tmem_ld128(tS, sv);
+
+      const float4* bj = reinterpret_cast<const float4*>(sBias + (s * 2 + t) * kAttnBN);
+      float mx = -INFINITY;
+      const bool diag = (j == diag_blk);
+#pragma unroll
+      for (int c4 = 0; c4 < 32; ++c4) {
+        const float4 bb = bj[c4];
+        float x0 = fmaf(__uint_as_float(sv[4 * c4 + 0]), rowscale, bb.x);
+        float x1 = fmaf(__uint_as_float(sv[4 * c4 + 1]), rowscale, bb.y);
+        float x2 = fmaf(__uint_as_float(sv[4 * c4 + 2]), rowscale, bb.z);
+        float x3 = fmaf(__uint_as_float(sv[4 * c4 + 3]), rowscale, bb.w);
+        if (diag) {
+          const int c = 4 * c4;
+          if (c + 0 > r) x0 = -INFINITY;
+          if (c + 1 > r) x1 = -INFINITY;
+          if (c + 2 > r) x2 = -INFINITY;
+          if (c + 3 > r) x3 = -INFINITY;
+        }
+        sv[4 * c4 + 0] = __float_as_uint(x0);
+        sv[4 * c4 + 1] = __float_as_uint(x1);
+        sv[4 * c4 + 2] = __float_as_uint(x2);
+        sv[4 * c4 + 3] = __float_as_uint(x3);
+        mx = fmaxf(mx, fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)));
+      }
+
+      // lazy max: move it (and rescale O) only when it grows by more than 8 in
+      // log2 units; O is stable here because S_t(j) completing implies the
+      // P_t(j-1) V MMA, issued earlier, completed too.
+      const float m_new = fmaxf(m_run, mx);
+      bool need = false;
+      float alpha = 1.f;
+      if (j == 0) {
+        m_run = m_new;
+      } else if (m_new > m_run + 8.0f) {
+        need = true;
+        alpha = ex2_approx(m_run - m_new);
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      const float msub = (m_run == -INFINITY) ? 0.f : m_run;
+      uint32_t pk[64];
+      float lsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = ex2_approx(__uint_as_float(sv[2 * c]) - msub);
+        const float p1 = ex2_approx(__uint_as_float(sv[2 * c + 1]) - msub);
+        lsum += p0 + p1;
+        pk[c] = pack_bf16x2(p0, p1);
+      }
+      l_run += lsum;
+      tmem_st64(tS, pk);
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_P_FULL + t));
+    }
+
+    if (ok && me.nblk > 0) {
+      if (warp_wait(bar(BAR_O_FULL + t), 0, p.err, ERR_ATTN_O_FULL)) {
+        tc_fence_after();
+        const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+        const bool valid = i < p.Sq;
+        __nv_bfloat16* orow =
+            p.out + (int64_t)b * p.o_sb + (int64_t)i * p.o_ss + (int64_t)me.head * p.o_sh;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          uint4 w[4];
+          uint32_t* wp = reinterpret_cast<uint32_t*>(w);
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            wp[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv_l,
+                                __uint_as_float(o[2 * e + 1]) * inv_l);
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[e] = w[e];
+          }
+        }
+        if (valid && p.lse != nullptr) {
+          const float lse2 = (l_run > 0.f) ? (m_run + __log2f(l_run)) : -INFINITY;
+          p.lse[(int64_t)b * p.lse_sb + (int64_t)me.head * p.lse_sh + i] =
+              lse2 * 0.6931471805599453f;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tg

@@ -1,0 +1,379 @@
+// C ABI of the tokengate_b200 kernels (declared in include/tokengate_b200.h).
+//
+// One translation unit: the kernels live in the .cuh files included below,
+// so the library has a single device error word and no relocatable device
+// code. Host code here validates arguments, encodes TMA tensor maps through
+// the driver entry point (no libcuda link), and launches on the caller's
+// stream. Nothing here allocates device memory.
+#include <cstdio>
+#include <cstring>
+#include <cstdarg>
+#include <mutex>
+
+#include "../../include/tokengate_b200.h"
+#include "ptx.cuh"
+#include "keybias_attn.cuh"
+#include "gate_score.cuh"
+#include "topk_select.cuh"
+#include "gather_rows.cuh"
+
+// Bit flags set by kernels whose bounded waits gave up (see ptx.cuh).
+__device__ unsigned int g_tg_device_error = 0;
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(TG_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+unsigned int* g_err_ptr[kMaxDevices] = {};
+bool g_attn_attr_set[kMaxDevices] = {};
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(TG_ERR_UNSUPPORTED, "device index %d", *dev);
+  return TG_OK;
+}
+
+// Device address of g_tg_device_error on the current device.
+int device_error_ptr(unsigned int** out) {
+  int dev;
+  int st = current_device(&dev);
+  if (st) return st;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_err_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_tg_device_error);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_tg_device_error)");
+    g_err_ptr[dev] = static_cast<unsigned int*>(p);
+  }
+  *out = g_err_ptr[dev];
+  return TG_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode_fn(EncodeTiledFn* fn) {
+  static EncodeTiledFn cached = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) cached = (EncodeTiledFn)p;
+  });
+  if (cached == nullptr)
+    return fail(TG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(err));
+  *fn = cached;
+  return TG_OK;
+}
+
+// (B, S, H, 128) bf16 tensor with element strides -> 4-D map over (d, h, s, b),
+// box (64, 1, 128, 1), 128-byte swizzle, zero fill out of bounds.
+int encode_bshd(CUtensorMap* map, const void* base, int B, int S, int H, int64_t sb, int64_t ss,
+                int64_t sh, const char* name) {
+  EncodeTiledFn enc = nullptr;
+  int st = get_encode_fn(&enc);
+  if (st) return st;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return fail(TG_ERR_ALIGNMENT, "%s: base address not 16-byte aligned", name);
+  if (B == 1) sb = ss * S;  // unused coordinate: any legal stride
+  if (H == 1) sh = 128;
+  const int64_t bytes[3] = {sh * 2, ss * 2, sb * 2};
+  for (int i = 0; i < 3; ++i)
+    if (bytes[i] <= 0 || (bytes[i] & 15) != 0 || bytes[i] >= (int64_t(1) << 40))
+      return fail(TG_ERR_ALIGNMENT,
+                  "%s: head/row/batch strides (%lld, %lld, %lld elements) must be positive "
+                  "multiples of 8",
+                  name, (long long)sh, (long long)ss, (long long)sb);
+  cuuint64_t dims[4] = {128, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)bytes[0], (cuuint64_t)bytes[1], (cuuint64_t)bytes[2]};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TG_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return TG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tg_abi_version(void) { return TG_ABI_VERSION; }
+
+const char* tg_last_error(void) { return g_last_error; }
+
+int tg_device_error(void* stream, unsigned int* flags_out, int clear) {
+  if (flags_out == nullptr) return fail(TG_ERR_INVALID_ARGUMENT, "flags_out is NULL");
+  unsigned int* dptr;
+  int st = device_error_ptr(&dptr);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(flags_out, dptr, sizeof(unsigned int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  if (clear) {
+    e = cudaMemsetAsync(dptr, 0, sizeof(unsigned int), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the device error word");
+  }
+  return TG_OK;
+}
+
+int tg_keybias_attn_fwd(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, const void* k,
+                        int64_t k_sb, int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sb,
+                        int64_t v_ss, int64_t v_sh, const float* bias, int64_t bias_sb,
+                        int64_t bias_sh, const float* q_row_scale, int64_t qs_sb, int64_t qs_sh,
+                        void* out, int64_t o_sb, int64_t o_ss, int64_t o_sh, float* lse,
+                        int64_t lse_sb, int64_t lse_sh, int B, int Sq, int Sk, int Hq, int Hkv,
+                        int D, float softmax_scale, int causal, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "q, k, v and out must be non-NULL");
+  if (B < 1 || Sq < 1 || Sk < 1 || Hq < 1 || Hkv < 1)
+    return fail(TG_ERR_INVALID_ARGUMENT, "empty problem: B=%d Sq=%d Sk=%d Hq=%d Hkv=%d", B, Sq, Sk,
+                Hq, Hkv);
+  if (B > 65535) return fail(TG_ERR_UNSUPPORTED, "B=%d exceeds 65535", B);
+  if (D != 128) return fail(TG_ERR_UNSUPPORTED, "head_dim %d not served (only 128)", D);
+  if (Hq % Hkv != 0)
+    return fail(TG_ERR_INVALID_ARGUMENT, "query heads %d not a multiple of kv heads %d", Hq, Hkv);
+  if (causal && Sq != Sk)
+    return fail(TG_ERR_INVALID_ARGUMENT, "causal attention needs Sq == Sk (got %d, %d)", Sq, Sk);
+  if (!(softmax_scale > 0.f)) return fail(TG_ERR_INVALID_ARGUMENT, "softmax_scale must be > 0");
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (o_ss & 7) || (o_sh & 7) || (o_sb & 7))
+    return fail(TG_ERR_ALIGNMENT, "out: base 16-byte aligned and strides multiples of 8 needed");
+
+  CUtensorMap tq, tk, tv;
+  int st;
+  if ((st = encode_bshd(&tq, q, B, Sq, Hq, q_sb, q_ss, q_sh, "q"))) return st;
+  if ((st = encode_bshd(&tk, k, B, Sk, Hkv, k_sb, k_ss, k_sh, "k"))) return st;
+  if ((st = encode_bshd(&tv, v, B, Sk, Hkv, v_sb, v_ss, v_sh, "v"))) return st;
+
+  tg::AttnParams p;
+  memset(&p, 0, sizeof(p));
+  p.bias = bias;
+  p.bias_sb = bias_sb;
+  p.bias_sh = bias_sh;
+  p.qscale = q_row_scale;
+  p.qs_sb = qs_sb;
+  p.qs_sh = qs_sh;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.o_sb = o_sb;
+  p.o_ss = o_ss;
+  p.o_sh = o_sh;
+  p.lse = lse;
+  p.lse_sb = lse_sb;
+  p.lse_sh = lse_sh;
+  p.B = B;
+  p.Sq = Sq;
+  p.Sk = Sk;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.G = Hq / Hkv;
+  p.pair_heads = (p.G % 2 == 0) ? 1 : 0;
+  p.causal = causal ? 1 : 0;
+  p.n_mblocks = (Sq + tg::kAttnBM - 1) / tg::kAttnBM;
+  p.n_kblocks = (Sk + tg::kAttnBN - 1) / tg::kAttnBN;
+  p.heads_per_unit_row = p.pair_heads ? Hq / 2 : Hq;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  if ((st = device_error_ptr(&p.err))) return st;
+
+  const int64_t units =
+      p.pair_heads ? (int64_t)p.n_mblocks * (Hq / 2) : (int64_t)((p.n_mblocks + 1) / 2) * Hq;
+  if (units > 0x7fffffff) return fail(TG_ERR_UNSUPPORTED, "problem too large");
+
+  int dev;
+  if ((st = current_device(&dev))) return st;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_attn_attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(tg::keybias_attn_fwd_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           tg::kAttnSmemBytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention smem)");
+      g_attn_attr_set[dev] = true;
+    }
+  }
+  dim3 grid((unsigned)units, (unsigned)B);
+  tg::keybias_attn_fwd_kernel<<<grid, tg::kAttnThreads, tg::kAttnSmemBytes,
+                                static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "keybias attention launch");
+  return TG_OK;
+}
+
+int tg_gate_score(const void* hidden, int64_t h_sb, int64_t h_ss, int hidden_dim, const float* w,
+                  int B, const int32_t* row_begin, const int32_t* row_count, float* scores,
+                  int64_t s_sb, void* stream) {
+  if (hidden == nullptr || w == nullptr || scores == nullptr || row_begin == nullptr ||
+      row_count == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (B < 1) return fail(TG_ERR_INVALID_ARGUMENT, "B=%d", B);
+  const int nv = hidden_dim / 256;
+  if (hidden_dim % 256 != 0 ||
+      !(nv == 1 || nv == 2 || nv == 4 || nv == 8 || nv == 10 || nv == 16 || nv == 20))
+    return fail(TG_ERR_UNSUPPORTED,
+                "hidden_dim %d not served (256, 512, 1024, 2048, 2560, 4096, 5120)", hidden_dim);
+  if ((reinterpret_cast<uintptr_t>(hidden) & 15) || (h_ss & 7) || (h_sb & 7) ||
+      (reinterpret_cast<uintptr_t>(w) & 15))
+    return fail(TG_ERR_ALIGNMENT, "hidden rows and w must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int b0 = 0; b0 < B; b0 += tg::kScoreMaxReq) {
+    const int nb = B - b0 < tg::kScoreMaxReq ? B - b0 : tg::kScoreMaxReq;
+    tg::ScoreParams p;
+    memset(&p, 0, sizeof(p));
+    p.h = static_cast<const __nv_bfloat16*>(hidden) + (int64_t)b0 * h_sb;
+    p.h_sb = h_sb;
+    p.h_ss = h_ss;
+    p.w = w;
+    p.out = scores + (int64_t)b0 * s_sb;
+    p.out_sb = s_sb;
+    p.B = nb;
+    p.row_off[0] = 0;
+    for (int i = 0; i < nb; ++i) {
+      if (row_begin[b0 + i] < 0 || row_count[b0 + i] < 0)
+        return fail(TG_ERR_INVALID_ARGUMENT, "negative row range for request %d", b0 + i);
+      p.begin[i] = row_begin[b0 + i];
+      p.row_off[i + 1] = p.row_off[i] + row_count[b0 + i];
+    }
+    p.total_rows = p.row_off[nb];
+    if (p.total_rows == 0) continue;
+    const int64_t warps_needed = p.total_rows;
+    int64_t blocks = (warps_needed + 7) / 8;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    switch (nv) {
+      case 1: tg::gate_score_kernel<1><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+      case 2: tg::gate_score_kernel<2><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+      case 4: tg::gate_score_kernel<4><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+      case 8: tg::gate_score_kernel<8><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+      case 10: tg::gate_score_kernel<10><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+      case 16: tg::gate_score_kernel<16><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+      default: tg::gate_score_kernel<20><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "gate score launch");
+  }
+  return TG_OK;
+}
+
+int tg_topk_select(const float* scores, int64_t s_sb, int B, const int32_t* n_state,
+                   const int32_t* k, const int32_t* state_begin, const int32_t* seq_len,
+                   int n_alloc, int64_t* keep, int64_t keep_sb, void* bias_out, int64_t bias_sb,
+                   int bias_dtype, int64_t* topk_local, int64_t tl_sb, void* stream) {
+  if (scores == nullptr || keep == nullptr || n_state == nullptr || k == nullptr ||
+      state_begin == nullptr || seq_len == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (B < 1 || n_alloc < 1) return fail(TG_ERR_INVALID_ARGUMENT, "B=%d n_alloc=%d", B, n_alloc);
+  if (bias_out != nullptr && bias_dtype != 0 && bias_dtype != 1)
+    return fail(TG_ERR_INVALID_ARGUMENT, "bias_dtype %d (0 = fp32, 1 = bf16)", bias_dtype);
+  for (int b = 0; b < B; ++b) {
+    const int n = n_state[b], kk = k[b], s0 = state_begin[b], L = seq_len[b];
+    if (n < 1 || kk < 1 || kk > n)
+      return fail(TG_ERR_INVALID_ARGUMENT, "request %d: need 1 <= k (%d) <= n_state (%d)", b, kk, n);
+    if (s0 < 0 || s0 + n > L)
+      return fail(TG_ERR_INVALID_ARGUMENT, "request %d: state [%d, %d) outside seq_len %d", b, s0,
+                  s0 + n, L);
+    const int n_kept = s0 + kk + (L - s0 - n);
+    if (n_kept > n_alloc)
+      return fail(TG_ERR_INVALID_ARGUMENT, "request %d: n_kept %d exceeds n_alloc %d", b, n_kept,
+                  n_alloc);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int b0 = 0; b0 < B; b0 += tg::kTopkMaxReq) {
+    const int nb = B - b0 < tg::kTopkMaxReq ? B - b0 : tg::kTopkMaxReq;
+    tg::TopkParams p;
+    memset(&p, 0, sizeof(p));
+    p.scores = scores + (int64_t)b0 * s_sb;
+    p.s_sb = s_sb;
+    p.keep = keep + (int64_t)b0 * keep_sb;
+    p.keep_sb = keep_sb;
+    p.bias_dtype = bias_dtype;
+    p.bias_sb = bias_sb;
+    if (bias_out != nullptr)
+      p.bias_out = static_cast<char*>(bias_out) + (int64_t)b0 * bias_sb * (bias_dtype ? 2 : 4);
+    p.topk_local = topk_local ? topk_local + (int64_t)b0 * tl_sb : nullptr;
+    p.tl_sb = tl_sb;
+    p.n_alloc = n_alloc;
+    for (int i = 0; i < nb; ++i) {
+      p.n_state[i] = n_state[b0 + i];
+      p.k[i] = k[b0 + i];
+      p.begin[i] = state_begin[b0 + i];
+      p.seq_len[i] = seq_len[b0 + i];
+    }
+    tg::topk_select_kernel<<<nb, tg::kTopkThreads, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "top-k launch");
+  }
+  return TG_OK;
+}
+
+int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t* idx,
+                   int64_t idx_sb, int B, int n_rows, const int32_t* n_valid, void* stream) {
+  if (tensors == nullptr || idx == nullptr || n_valid == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (n_tensors < 1 || n_tensors > TG_MAX_GATHER_TENSORS)
+    return fail(TG_ERR_INVALID_ARGUMENT, "n_tensors %d (1..%d)", n_tensors, TG_MAX_GATHER_TENSORS);
+  if (B < 1 || n_rows < 0) return fail(TG_ERR_INVALID_ARGUMENT, "B=%d n_rows=%d", B, n_rows);
+  if (n_rows == 0) return TG_OK;
+  for (int i = 0; i < n_tensors; ++i) {
+    const tg_gather_tensor& t = tensors[i];
+    if (t.src == nullptr || t.dst == nullptr)
+      return fail(TG_ERR_INVALID_ARGUMENT, "tensor %d: NULL pointer", i);
+    if (t.n_seg < 1 || t.seg_bytes < 16)
+      return fail(TG_ERR_INVALID_ARGUMENT, "tensor %d: n_seg %d seg_bytes %lld", i, t.n_seg,
+                  (long long)t.seg_bytes);
+    const int64_t m = (reinterpret_cast<uintptr_t>(t.src) | reinterpret_cast<uintptr_t>(t.dst) |
+                       t.src_batch_stride | t.src_row_stride | t.src_seg_stride |
+                       t.dst_batch_stride | t.dst_row_stride | t.dst_seg_stride | t.seg_bytes);
+    if (m & 15) return fail(TG_ERR_ALIGNMENT, "tensor %d: addresses/strides/seg_bytes not 16-byte multiples", i);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int b0 = 0; b0 < B; b0 += tg::kGatherMaxReq) {
+    const int nb = B - b0 < tg::kGatherMaxReq ? B - b0 : tg::kGatherMaxReq;
+    tg::GatherParams p;
+    memset(&p, 0, sizeof(p));
+    for (int i = 0; i < n_tensors; ++i) {
+      p.t[i] = tensors[i];
+      p.t[i].src = static_cast<const char*>(tensors[i].src) + (int64_t)b0 * tensors[i].src_batch_stride;
+      p.t[i].dst = static_cast<char*>(tensors[i].dst) + (int64_t)b0 * tensors[i].dst_batch_stride;
+    }
+    p.n_tensors = n_tensors;
+    p.idx = idx + (int64_t)b0 * idx_sb;
+    p.idx_sb = idx_sb;
+    p.n_rows = n_rows;
+    p.B = nb;
+    for (int i = 0; i < nb; ++i) {
+      if (n_valid[b0 + i] < 0 || n_valid[b0 + i] > n_rows)
+        return fail(TG_ERR_INVALID_ARGUMENT, "n_valid[%d]=%d outside [0, %d]", b0 + i,
+                    n_valid[b0 + i], n_rows);
+      p.n_valid[i] = n_valid[b0 + i];
+    }
+    const int64_t warps = (int64_t)nb * n_tensors * n_rows;
+    int64_t blocks = (warps + 7) / 8;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    tg::gather_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+  }
+  return TG_OK;
+}
+
+}  // extern "C"

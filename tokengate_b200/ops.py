@@ -1,0 +1,290 @@
+"""Torch-facing wrappers of the four hot-path kernels.
+
+Each wrapper validates tensors, takes raw pointers and strides, and calls the
+C ABI on the current CUDA stream of the tensors' device. All outputs are
+allocated here by torch (the C ABI allocates nothing). No wrapper has a CPU
+or eager fallback: CPU tensors, a missing library or an unsupported shape
+raise.
+"""
+from typing import Optional, Sequence, Tuple
+
+import contextlib
+import ctypes
+
+import torch
+
+from . import _lib
+
+_LOG2E = 1.4426950408889634
+
+
+def _require_cuda(name: str, t: torch.Tensor, dtype: Optional[torch.dtype] = None) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the B200 kernels have no CPU path), "
+                         f"got {t.device}")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def _device_ctx(t: torch.Tensor):
+    if torch.cuda.current_device() == t.device.index:
+        return contextlib.nullcontext()
+    return torch.cuda.device(t.device)
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _i32_array(values: Sequence[int]):
+    arr = (ctypes.c_int32 * len(values))(*[int(v) for v in values])
+    return arr
+
+
+# ----------------------------------------------------------------- attention
+def keybias_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      bias: Optional[torch.Tensor] = None,
+                      softmax_scale: Optional[float] = None,
+                      causal: bool = True,
+                      q_row_scale: Optional[torch.Tensor] = None,
+                      return_lse: bool = False,
+                      out: Optional[torch.Tensor] = None):
+    """softmax(scale * q k^T + bias) v with causal masking and GQA.
+
+    q: (B, Sq, Hq, 128) bf16, k/v: (B, Sk, Hkv, 128) bf16, any strides with a
+    contiguous last dim (the (B, H, S, D) views the reference passes are the
+    transposes of these). bias: fp32, broadcastable to (B, Hq, Sk) with a
+    contiguous last dim, in score units (what the FlexAttention score_mod
+    adds). q_row_scale: fp32 broadcastable to (B, Hq, Sq) with a contiguous
+    last dim. Returns out (B, Sq, Hq, 128) bf16, and lse (B, Hq, Sq) fp32 when
+    return_lse.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(name, t, torch.bfloat16)
+        if t.dim() != 4 or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be 4-D (B, S, H, D) with a contiguous last dim")
+    B, Sq, Hq, D = q.shape
+    Sk, Hkv = k.shape[1], k.shape[2]
+    if k.shape[0] != B or v.shape[:3] != k.shape[:3] or k.shape[3] != D or v.shape[3] != D:
+        raise ValueError(f"shape mismatch: q {tuple(q.shape)} k {tuple(k.shape)} v {tuple(v.shape)}")
+    if not (q.device == k.device == v.device):
+        raise ValueError("q, k, v must be on one device")
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    if out is None:
+        out = torch.empty((B, Sq, Hq, D), dtype=torch.bfloat16, device=q.device)
+    else:
+        _require_cuda("out", out, torch.bfloat16)
+        if tuple(out.shape) != (B, Sq, Hq, D) or out.stride(-1) != 1:
+            raise ValueError("out must be (B, Sq, Hq, D) with a contiguous last dim")
+    lse = torch.empty((B, Hq, Sq), dtype=torch.float32, device=q.device) if return_lse else None
+
+    bias_ptr, bsb, bsh = None, 0, 0
+    if bias is not None:
+        _require_cuda("bias", bias, torch.float32)
+        bb = bias
+        while bb.dim() < 3:
+            bb = bb.unsqueeze(0)
+        if bb.dim() != 3 or bb.shape[-1] != Sk or bb.stride(-1) != 1:
+            raise ValueError(f"bias must broadcast to (B, Hq, Sk)=({B}, {Hq}, {Sk}) with a "
+                             f"contiguous last dim, got {tuple(bias.shape)}")
+        if bb.shape[0] not in (1, B) or bb.shape[1] not in (1, Hq):
+            raise ValueError(f"bias shape {tuple(bias.shape)} does not broadcast to ({B}, {Hq}, {Sk})")
+        bsb = 0 if bb.shape[0] == 1 else bb.stride(0)
+        bsh = 0 if bb.shape[1] == 1 else bb.stride(1)
+        bias_ptr = bb.data_ptr()
+    qs_ptr, qsb, qsh = None, 0, 0
+    if q_row_scale is not None:
+        _require_cuda("q_row_scale", q_row_scale, torch.float32)
+        qq = q_row_scale
+        while qq.dim() < 3:
+            qq = qq.unsqueeze(0)
+        if qq.shape[-1] != Sq or qq.stride(-1) != 1 or qq.shape[0] not in (1, B) \
+                or qq.shape[1] not in (1, Hq):
+            raise ValueError(f"q_row_scale must broadcast to ({B}, {Hq}, {Sq}) with a contiguous last dim")
+        qsb = 0 if qq.shape[0] == 1 else qq.stride(0)
+        qsh = 0 if qq.shape[1] == 1 else qq.stride(1)
+        qs_ptr = qq.data_ptr()
+
+    L = _lib.lib()
+    with _device_ctx(q):
+        _lib.check(L.tg_keybias_attn_fwd(
+            q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
+            k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+            v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
+            bias_ptr, bsb, bsh,
+            qs_ptr, qsb, qsh,
+            out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+            lse.data_ptr() if lse is not None else None,
+            lse.stride(0) if lse is not None else 0, lse.stride(1) if lse is not None else 0,
+            B, Sq, Sk, Hq, Hkv, D, float(softmax_scale), int(bool(causal)), _stream(q)))
+    return (out, lse) if return_lse else out
+
+
+# ----------------------------------------------------------------- gate score
+def gate_score(hidden: torch.Tensor, w: torch.Tensor, row_begin: Sequence[int],
+               row_count: Sequence[int], out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """scores[b, r] = logsigmoid(w . hidden[b, row_begin[b] + r]) for r < row_count[b].
+
+    hidden: (B, S, H) bf16 with a contiguous last dim; w: (H,) fp32 contiguous.
+    Returns fp32 (B, max(row_count)); entries past row_count[b] are untouched
+    (zero when the output is allocated here).
+    """
+    _require_cuda("hidden", hidden, torch.bfloat16)
+    _require_cuda("w", w, torch.float32)
+    if hidden.dim() != 3 or hidden.stride(-1) != 1:
+        raise ValueError("hidden must be (B, S, H) with a contiguous last dim")
+    B, S, H = hidden.shape
+    if w.dim() != 1 or w.shape[0] != H or not w.is_contiguous():
+        raise ValueError(f"w must be a contiguous ({H},) vector")
+    if len(row_begin) != B or len(row_count) != B:
+        raise ValueError("row_begin / row_count need one entry per request")
+    for b in range(B):
+        if row_begin[b] < 0 or row_count[b] < 0 or row_begin[b] + row_count[b] > S:
+            raise ValueError(f"request {b}: rows [{row_begin[b]}, {row_begin[b] + row_count[b]}) "
+                             f"outside [0, {S})")
+    n_max = max(int(c) for c in row_count)
+    if out is None:
+        out = torch.zeros((B, max(n_max, 1)), dtype=torch.float32, device=hidden.device)
+    else:
+        _require_cuda("out", out, torch.float32)
+        if out.dim() != 2 or out.shape[0] != B or out.shape[1] < n_max or out.stride(1) != 1:
+            raise ValueError("out must be (B, >= max(row_count)) fp32 with a contiguous last dim")
+    L = _lib.lib()
+    with _device_ctx(hidden):
+        _lib.check(L.tg_gate_score(hidden.data_ptr(), hidden.stride(0), hidden.stride(1), H,
+                                   w.data_ptr(), B, _i32_array(row_begin), _i32_array(row_count),
+                                   out.data_ptr(), out.stride(0), _stream(hidden)))
+    return out
+
+
+# ----------------------------------------------------------------- top-K
+def topk_select(scores: torch.Tensor, n_state: Sequence[int], k: Sequence[int],
+                state_begin: Sequence[int], seq_len: Sequence[int], n_alloc: int,
+                bias_dtype: Optional[torch.dtype] = torch.bfloat16,
+                want_topk_local: bool = False,
+                keep_out: Optional[torch.Tensor] = None,
+                bias_out: Optional[torch.Tensor] = None):
+    """Top-k state tokens per request (score desc, index asc) and the kept positions.
+
+    scores: fp32 (B, >= n_state[b]) with a contiguous last dim. k[b] is
+    K_clamped. Returns (keep int64 (B, n_alloc), bias (B, n_alloc) in
+    bias_dtype or None, topk_local int64 (B, max k) or None).
+    """
+    _require_cuda("scores", scores, torch.float32)
+    if scores.dim() != 2 or scores.stride(1) != 1:
+        raise ValueError("scores must be 2-D with a contiguous last dim")
+    B = scores.shape[0]
+    for name, arr in (("n_state", n_state), ("k", k), ("state_begin", state_begin), ("seq_len", seq_len)):
+        if len(arr) != B:
+            raise ValueError(f"{name} needs one entry per request")
+    for b in range(B):
+        if n_state[b] > scores.shape[1]:
+            raise ValueError(f"request {b}: n_state {n_state[b]} exceeds the score row ({scores.shape[1]})")
+    dev = scores.device
+    keep = keep_out if keep_out is not None else torch.empty((B, n_alloc), dtype=torch.int64, device=dev)
+    if keep.dtype != torch.int64 or keep.shape[0] != B or keep.shape[1] < n_alloc or keep.stride(1) != 1:
+        raise ValueError("keep_out must be int64 (B, >= n_alloc) with a contiguous last dim")
+    bias = None
+    dt_code = 0
+    if bias_dtype is not None or bias_out is not None:
+        if bias_out is not None:
+            bias = bias_out
+        else:
+            bias = torch.empty((B, n_alloc), dtype=bias_dtype, device=dev)
+        if bias.dtype not in (torch.float32, torch.bfloat16) or bias.stride(1) != 1:
+            raise ValueError("bias must be fp32 or bf16 with a contiguous last dim")
+        dt_code = 0 if bias.dtype == torch.float32 else 1
+    tl = None
+    if want_topk_local:
+        tl = torch.empty((B, max(int(x) for x in k)), dtype=torch.int64, device=dev)
+    L = _lib.lib()
+    with _device_ctx(scores):
+        _lib.check(L.tg_topk_select(
+            scores.data_ptr(), scores.stride(0), B, _i32_array(n_state), _i32_array(k),
+            _i32_array(state_begin), _i32_array(seq_len), int(n_alloc),
+            keep.data_ptr(), keep.stride(0),
+            bias.data_ptr() if bias is not None else None, bias.stride(0) if bias is not None else 0,
+            dt_code, tl.data_ptr() if tl is not None else None, tl.stride(0) if tl is not None else 0,
+            _stream(scores)))
+    return keep, bias, tl
+
+
+# ----------------------------------------------------------------- gather
+def gather_spec_rows(src: torch.Tensor, dst: torch.Tensor, row_dim: int) -> _lib.GatherTensor:
+    """Describe a gather of src -> dst along `row_dim` (batch is dim 0).
+
+    The bytes of one row must be one contiguous block, or one contiguous
+    block per index of the dims between the batch and the row dim (e.g. a
+    (B, H, S, D) tensor gathered along S: one 256-byte segment per head).
+    """
+    if src.dtype != dst.dtype or src.device != dst.device:
+        raise ValueError("src and dst must share dtype and device")
+    if src.dim() != dst.dim() or src.dim() < 2:
+        raise ValueError("src and dst must have the same rank (>= 2)")
+    if not (1 <= row_dim < src.dim()):
+        raise ValueError("row_dim must be a non-batch dim")
+    es = src.element_size()
+    inner_src = src.shape[row_dim + 1:]
+    if tuple(dst.shape[row_dim + 1:]) != tuple(inner_src) or tuple(dst.shape[1:row_dim]) != tuple(src.shape[1:row_dim]):
+        raise ValueError(f"src {tuple(src.shape)} and dst {tuple(dst.shape)} differ outside the row dim")
+
+    def inner_block(t):
+        # the dims after row_dim must be contiguous (one block per segment)
+        expected = 1
+        for d in range(t.dim() - 1, row_dim, -1):
+            if t.shape[d] != 1 and t.stride(d) != expected:
+                raise ValueError("the dims after the row dim must be contiguous")
+            expected *= t.shape[d]
+        return expected
+
+    seg_elems = inner_block(src)
+    inner_block(dst)
+    mid = list(range(1, row_dim))
+    n_seg = 1
+    seg_stride_src = seg_stride_dst = 0
+    if mid:
+        if len(mid) > 1:
+            raise ValueError("at most one dim between the batch and the row dim")
+        n_seg = src.shape[mid[0]]
+        seg_stride_src = src.stride(mid[0]) * es
+        seg_stride_dst = dst.stride(mid[0]) * es
+    g = _lib.GatherTensor()
+    g.src = src.data_ptr()
+    g.dst = dst.data_ptr()
+    g.src_batch_stride = src.stride(0) * es
+    g.src_row_stride = src.stride(row_dim) * es
+    g.src_seg_stride = seg_stride_src
+    g.dst_batch_stride = dst.stride(0) * es
+    g.dst_row_stride = dst.stride(row_dim) * es
+    g.dst_seg_stride = seg_stride_dst
+    g.seg_bytes = seg_elems * es
+    g.n_seg = n_seg
+    g.reserved = 0
+    return g
+
+
+def gather_rows(specs: Sequence[_lib.GatherTensor], idx: torch.Tensor, n_valid: Sequence[int],
+                n_rows: int, device: torch.device) -> None:
+    """One launch: for every spec, dst row r <- src row idx[b, r] (r < n_valid[b]), zeros past it."""
+    _require_cuda("idx", idx, torch.int64)
+    if idx.dim() != 2 or idx.stride(1) != 1 or idx.shape[1] < n_rows:
+        raise ValueError("idx must be int64 (B, >= n_rows) with a contiguous last dim")
+    B = idx.shape[0]
+    if len(n_valid) != B:
+        raise ValueError("n_valid needs one entry per request")
+    n = len(specs)
+    if not 1 <= n <= _lib.MAX_GATHER_TENSORS:
+        raise ValueError(f"1..{_lib.MAX_GATHER_TENSORS} tensors per launch, got {n}")
+    arr = (_lib.GatherTensor * n)(*specs)
+    L = _lib.lib()
+    with _device_ctx(idx):
+        _lib.check(L.tg_gather_rows(arr, n, idx.data_ptr(), idx.stride(0), B, int(n_rows),
+                                    _i32_array(n_valid), _stream(idx)))
+
+
+def device_error(clear: bool = False) -> int:
+    """Flags recorded by kernels whose bounded waits gave up on the current device (synchronises)."""
+    return _lib.device_error(torch.cuda.current_stream().cuda_stream, clear)
