@@ -1,0 +1,155 @@
+"""CPU ORACLE (test infrastructure): the gated prefill in float32 torch on the CPU.
+
+Restates, independently of tokengate_b200's modules:
+  * the reference control flow prefill_batch_for_decode
+    (tokengate/e2e_gate/gate_module/gate_forward.py:1269-1579): right-padded
+    Phase 1 over layers 0..L, scoring of each request's state span
+    (:1396-1407), K_clamped = max(1, min(K, n_art)) (:1409-1410), selection +
+    sorted keep list (:84-99, :1417-1421), gather of kept hidden rows with
+    original positions (:1443-1461), Phase-2 gate bias = score at kept state
+    tokens, 0 elsewhere, -1e9 pads (:968-1036, :1463-1469), Phase 2 over
+    layers L+1..N-1 with RoPE at the kept positions (:1528-1553), head on the
+    last kept row (:1555-1562);
+  * the Qwen3 decoder math the reference runs through transformers
+    (RMSNorm, q/k RMSNorm, rotate-half RoPE, causal attention with the
+    additive key bias as in sdpa_compat.py:6-37, SwiGLU MLP, tied or untied
+    lm_head).
+Scores are logsigmoid(w . h) with h the float32 layer-L output, evaluated in
+float64 and rounded to float32; selection by (score desc, index asc).
+"""
+from typing import Dict, List, Sequence
+
+import torch
+
+from .select import topk_indices
+
+
+def _rms(x, w, eps):
+    v = x.pow(2).mean(-1, keepdim=True)
+    return w * (x * torch.rsqrt(v + eps))
+
+
+def _rope_cos_sin(positions: torch.Tensor, head_dim: int, theta: float):
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    f = positions.to(torch.float64)[..., None] * inv            # (B, S, D/2)
+    emb = torch.cat([f, f], dim=-1)
+    return emb.cos().float(), emb.sin().float()
+
+
+def _rot_half(x):
+    h = x.shape[-1] // 2
+    return torch.cat([-x[..., h:], x[..., :h]], dim=-1)
+
+
+def _attention(q, k, v, bias_bs, chunk=256):
+    """q (B,S,Hq,D), k/v (B,S,Hkv,D) fp32, bias_bs (B,S) or None; causal."""
+    B, S, Hq, D = q.shape
+    G = Hq // k.shape[2]
+    kk = k.repeat_interleave(G, dim=2).permute(0, 2, 3, 1)     # (B, Hq, D, S)
+    vv = v.repeat_interleave(G, dim=2).permute(0, 2, 1, 3)     # (B, Hq, S, D)
+    qq = q.permute(0, 2, 1, 3)                                 # (B, Hq, S, D)
+    out = torch.empty_like(qq)
+    keys = torch.arange(S)
+    for c0 in range(0, S, chunk):
+        c1 = min(S, c0 + chunk)
+        s = (qq[:, :, c0:c1] @ kk) * (D ** -0.5)
+        if bias_bs is not None:
+            s = s + bias_bs[:, None, None, :]
+        s = s.masked_fill(keys[None, None, None, :] > torch.arange(c0, c1)[None, None, :, None],
+                          float("-inf"))
+        out[:, :, c0:c1] = torch.softmax(s, dim=-1) @ vv
+    return out.permute(0, 2, 1, 3)
+
+
+def _layer(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs):
+    B, S, _ = h.shape
+    D = cfg["head_dim"]
+    eps = cfg["rms_norm_eps"]
+    x = _rms(h, p["input_layernorm.weight"], eps)
+    q = (x @ p["self_attn.q_proj.weight"].T).view(B, S, -1, D)
+    k = (x @ p["self_attn.k_proj.weight"].T).view(B, S, -1, D)
+    v = (x @ p["self_attn.v_proj.weight"].T).view(B, S, -1, D)
+    q = _rms(q, p["self_attn.q_norm.weight"], eps)
+    k = _rms(k, p["self_attn.k_norm.weight"], eps)
+    c, s_ = cos[:, :, None, :], sin[:, :, None, :]
+    q = q * c + _rot_half(q) * s_
+    k = k * c + _rot_half(k) * s_
+    a = _attention(q, k, v, bias_bs).reshape(B, S, -1)
+    h = h + a @ p["self_attn.o_proj.weight"].T
+    x = _rms(h, p["post_attention_layernorm.weight"], eps)
+    g = x @ p["mlp.gate_proj.weight"].T
+    u = x @ p["mlp.up_proj.weight"].T
+    h = h + (torch.nn.functional.silu(g) * u) @ p["mlp.down_proj.weight"].T
+    return h
+
+
+def weights_fp32(model) -> (dict, dict):
+    """(per-layer param dicts, globals) as float32 CPU tensors, plus a config dict."""
+    sd = {k: v.detach().float().cpu() for k, v in model.state_dict().items()}
+    c = model.config
+    cfg = dict(head_dim=c.head_dim, rms_norm_eps=c.rms_norm_eps, rope_theta=c.rope_parameters["rope_theta"]
+               if getattr(c, "rope_parameters", None) else c.rope_theta,
+               n_layers=c.num_hidden_layers)
+    layers = []
+    for i in range(c.num_hidden_layers):
+        pre = f"model.layers.{i}."
+        layers.append({k[len(pre):]: v for k, v in sd.items() if k.startswith(pre)})
+    g = dict(embed=sd["model.embed_tokens.weight"], norm=sd["model.norm.weight"],
+             lm_head=sd.get("lm_head.weight", sd["model.embed_tokens.weight"]))
+    return layers, g, cfg
+
+
+def gated_prefill(model, w_gate: torch.Tensor, prompt_ids_list: Sequence[Sequence[int]],
+                  starts: Sequence[int], ends: Sequence[int], gate_layer: int, K,
+                  weights=None, bias_bf16: bool = False) -> dict:
+    """Returns dict(first_tokens (B,), kept_positions list, n_kepts, K_clampeds,
+    logits (B, vocab) fp32, scores list, phase1_hidden (B, S, H)).
+
+    bias_bf16: round the Phase-2 bias to bfloat16, as the reference does when
+    the model runs in bf16 (gate_bias_batched has the hidden dtype, :1450)."""
+    layers, g, cfg = weights if weights is not None else weights_fp32(model)
+    B = len(prompt_ids_list)
+    lens = [len(x) for x in prompt_ids_list]
+    S = max(lens)
+    ids = torch.zeros(B, S, dtype=torch.long)
+    for b, x in enumerate(prompt_ids_list):
+        ids[b, :lens[b]] = torch.as_tensor(list(x), dtype=torch.long)
+    h = g["embed"][ids]
+    pos = torch.arange(S).unsqueeze(0).expand(B, -1)
+    cos, sin = _rope_cos_sin(pos, cfg["head_dim"], cfg["rope_theta"])
+    for i in range(gate_layer + 1):
+        h = _layer(h, layers[i], cfg, cos, sin, None)
+    w64 = w_gate.detach().double().reshape(-1).cpu()
+    Ks = list(K) if isinstance(K, (list, tuple)) else [K] * B
+    kept, scores, n_kepts, K_cl = [], [], [], []
+    for b in range(B):
+        n_art = ends[b] - starts[b]
+        sc = torch.nn.functional.logsigmoid(h[b, starts[b]:ends[b]].double() @ w64).float()
+        kc = max(1, min(int(Ks[b]), n_art))
+        top = torch.as_tensor(topk_indices(sc.numpy(), kc), dtype=torch.long)
+        keep = torch.cat([torch.arange(starts[b]), starts[b] + top, torch.arange(ends[b], lens[b])])
+        kept.append(keep)
+        scores.append(sc)
+        n_kepts.append(len(keep))
+        K_cl.append(kc)
+    n_alloc = max(n_kepts)
+    hp = torch.zeros(B, n_alloc, h.shape[-1])
+    kp = torch.zeros(B, n_alloc, dtype=torch.long)
+    bias = torch.full((B, n_alloc), -1e9)
+    for b in range(B):
+        n = n_kepts[b]
+        hp[b, :n] = h[b, kept[b]]
+        kp[b, :n] = kept[b]
+        bias[b, :n] = 0.0
+        bias[b, starts[b]:starts[b] + K_cl[b]] = scores[b][kept[b][starts[b]:starts[b] + K_cl[b]] - starts[b]]
+    if bias_bf16:
+        bias = bias.to(torch.bfloat16).float()
+    phase1_hidden = h
+    cos2, sin2 = _rope_cos_sin(kp, cfg["head_dim"], cfg["rope_theta"])
+    for i in range(gate_layer + 1, cfg["n_layers"]):
+        hp = _layer(hp, layers[i], cfg, cos2, sin2, bias)
+    last = torch.stack([_rms(hp[b, n_kepts[b] - 1], g["norm"], cfg["rms_norm_eps"]) for b in range(B)])
+    logits = last @ g["lm_head"].T
+    return dict(first_tokens=logits.argmax(-1), kept_positions=[k.tolist() for k in kept],
+                n_kepts=n_kepts, K_clampeds=K_cl, logits=logits, scores=scores,
+                phase1_hidden=phase1_hidden, bias=bias)

@@ -1,0 +1,192 @@
+"""Public API: load_model(...) -> TokenGateModel; model.generate(ids, tok, max_kept_prefill_tokens=K).
+
+Mirrors the reference API (tokengate/inference.py:63-180) and its state-span
+helpers (tokengate/e2e_gate/gate_module/gate_forward.py:664-689):
+  * ids carry exactly one STATE_START_ID (-1001) ... STATE_END_ID (-1002) pair
+    marking the prunable document; split_state_span strips them and returns
+    (clean_ids, start, end), raising ValueError on malformed spans;
+  * generate runs the gated prefill on the B200 kernels and returns a
+    GenerateOutput with the same fields.
+
+Scope: the gated prefill (time to first token). Decoding further tokens
+after the prefill is not part of this build, so max_new_tokens must be 1.
+Checkpoint loading covers the linear log-sigmoid gate (a .pt holding
+{"state_dict": {"readout.weight": (1, hidden)}, "metadata": {...}}); released
+checkpoints with a scoring branch and LoRA adapters are not served.
+"""
+import os
+import time
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Union
+
+import torch
+
+from .gate import LinLogSigGate
+from .model import patch_model, set_attention_backends_for_layers
+from .prefill import prefill_batch_for_decode
+
+STATE_START_ID = -1001
+STATE_END_ID = -1002
+_NO_PRUNING = 10_000_000
+
+
+def split_state_span(ids: List[int]):
+    """Strip the state sentinels: ids -> (clean_ids, start, end) (gate_forward.py:669-689)."""
+    starts = [i for i, t in enumerate(ids) if t == STATE_START_ID]
+    ends = [i for i, t in enumerate(ids) if t == STATE_END_ID]
+    if len(starts) != 1 or len(ends) != 1 or starts[0] >= ends[0]:
+        raise ValueError(
+            "ids carry no valid state span: expected exactly one STATE_START_ID followed by one "
+            f"STATE_END_ID (produce ids with apply_chat_template(state=...)); found starts={starts} "
+            f"ends={ends}")
+    s, e = starts[0], ends[0]
+    clean = list(ids[:s]) + list(ids[s + 1:e]) + list(ids[e + 1:])
+    return clean, s, e - 1
+
+
+def with_state_span(prefix: Sequence[int], state: Sequence[int], suffix: Sequence[int]) -> List[int]:
+    """prefix + [STATE_START_ID] + state + [STATE_END_ID] + suffix."""
+    return list(prefix) + [STATE_START_ID] + list(state) + [STATE_END_ID] + list(suffix)
+
+
+@dataclass
+class GenerateOutput:
+    """Result of TokenGateModel.generate (one entry per input sequence)."""
+    answers: List[str]
+    n_kept: List[int]
+    n_state: List[int]
+    kept_pos: List[List[int]]
+    prefill_s: float
+    decode_s: float
+    token_ids: List[List[int]]
+
+
+class TokenGateModel:
+    """A base model + gate behind one object; attribute access falls through to the model."""
+
+    def __init__(self, model, gate, gate_layer: int, base_model: str):
+        self.model = model
+        self.gate = gate
+        self.gate_layer = gate_layer
+        self.base_model = base_model
+
+    def __getattr__(self, name):
+        return getattr(self.model, name)
+
+    def prefill(self, ids_clean, starts, ends, K, prune_below_gate: bool = False):
+        """The gated prefill on clean ids (no sentinels)."""
+        return prefill_batch_for_decode(self.model, self.gate, ids_clean, starts, ends,
+                                        self.gate_layer, K, prune_below_gate=prune_below_gate)
+
+    def generate(self, ids: Union[List[int], List[List[int]]], tokenizer=None, *,
+                 max_new_tokens: int = 1, max_kept_prefill_tokens: Optional[int] = None,
+                 streamer=None) -> GenerateOutput:
+        if max_new_tokens != 1:
+            raise NotImplementedError("the B200 build serves the gated prefill (first token); "
+                                      "decoding more tokens is outside it: pass max_new_tokens=1")
+        if ids and isinstance(ids[0], int):
+            ids = [ids]
+        split = [split_state_span(list(seq)) for seq in ids]
+        clean = [s[0] for s in split]
+        starts = [s[1] for s in split]
+        ends = [s[2] for s in split]
+        k = _NO_PRUNING if max_kept_prefill_tokens is None else max_kept_prefill_tokens
+        dev = next(self.model.parameters()).device
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        first, _cache, kept, n_kepts, _kc = self.prefill(clean, starts, ends, k)
+        first_host = first.cpu()
+        torch.cuda.synchronize(dev)
+        prefill_s = time.perf_counter() - t0
+        tokens = [[int(t)] for t in first_host[:, 0].tolist()]
+        if streamer is not None:
+            streamer.put(first_host)
+            streamer.end()
+        answers = [tokenizer.decode(t) if tokenizer is not None else "" for t in tokens]
+        kept_host = kept.cpu()
+        kept_pos = [kept_host[b, :n].tolist() for b, n in enumerate(n_kepts)]
+        return GenerateOutput(answers=answers, n_kept=list(n_kepts),
+                              n_state=[e - s for s, e in zip(starts, ends)], kept_pos=kept_pos,
+                              prefill_s=prefill_s, decode_s=0.0, token_ids=tokens)
+
+
+# Qwen3 shapes named by BASELINE's configs (random-init, no checkpoints offline)
+QWEN3_SHAPES = {
+    "qwen3-1.7b": dict(hidden_size=2048, intermediate_size=6144, num_hidden_layers=28,
+                       num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                       rope_theta=1e6, vocab_size=151936, tie_word_embeddings=True,
+                       max_position_embeddings=40960),
+    "qwen3-8b": dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+                     num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                     rope_theta=1e6, vocab_size=151936, tie_word_embeddings=False,
+                     max_position_embeddings=131072),
+}
+
+
+def qwen3_config(name_or_dict):
+    from transformers.models.qwen3.configuration_qwen3 import Qwen3Config
+    kw = dict(QWEN3_SHAPES[name_or_dict]) if isinstance(name_or_dict, str) else dict(name_or_dict)
+    cfg = Qwen3Config(**kw)
+    cfg._attn_implementation = "eager"
+    return cfg
+
+
+def synthetic_qwen3(name_or_dict, seed: int = 0, device="cuda", dtype=torch.bfloat16):
+    """Random-init Qwen3ForCausalLM of a named shape, built directly on `device`."""
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3ForCausalLM
+    cfg = qwen3_config(name_or_dict)
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Qwen3ForCausalLM(cfg)
+    return model.to(dtype).eval()
+
+
+def load_model(checkpoint: Optional[str] = None, base_model=None, gate_layer: Optional[int] = None,
+               gate_attn: str = "b200", dtype=None, *, model: Optional[torch.nn.Module] = None,
+               gate: Optional[torch.nn.Module] = None, device="cuda", seed: int = 0) -> TokenGateModel:
+    """Build a TokenGateModel on the B200 kernels.
+
+    checkpoint : gate .pt ({"state_dict", "metadata"}) of a linear log-sigmoid
+        gate, or None when `gate` is passed (or for a random gate from `seed`).
+    base_model : a QWEN3_SHAPES name / Qwen3Config kwargs (random init from
+        `seed`), or a HF model id / path loadable by AutoModelForCausalLM;
+        ignored when `model` is passed. Read from the checkpoint metadata when
+        omitted, as in the reference.
+    gate_layer : the gate's layer (metadata when omitted).
+    gate_attn  : "b200" (or the reference's default name "fa2", same kernel).
+    """
+    if dtype is None:
+        dtype = torch.bfloat16
+    if dtype != torch.bfloat16:
+        raise NotImplementedError("the B200 kernels compute in bf16")
+    meta = {}
+    state = None
+    if checkpoint is not None:
+        if not os.path.isfile(checkpoint):
+            raise FileNotFoundError(f"gate checkpoint not found: {checkpoint}")
+        blob = torch.load(checkpoint, map_location="cpu", weights_only=False)
+        meta = blob.get("metadata", {})
+        state = blob.get("state_dict", blob)
+    if base_model is None:
+        base_model = meta.get("base_model")
+    if gate_layer is None:
+        gate_layer = meta.get("gate_layer")
+        if gate_layer is None:
+            raise ValueError("no gate_layer: pass gate_layer= or use a checkpoint that records it")
+    if model is None:
+        if base_model is None:
+            raise ValueError("no base_model: pass base_model= (a shape name, config kwargs or HF id)")
+        if isinstance(base_model, (dict,)) or base_model in QWEN3_SHAPES:
+            model = synthetic_qwen3(base_model, seed=seed, device=device, dtype=dtype)
+        else:
+            from transformers import AutoModelForCausalLM
+            model = AutoModelForCausalLM.from_pretrained(base_model, dtype=dtype).to(device).eval()
+    hidden = model.config.hidden_size
+    if gate is None:
+        gate = LinLogSigGate(hidden, generator=torch.Generator().manual_seed(seed + 1))
+        if state is not None:
+            gate.load_state_dict(state)
+    patch_model(model)
+    set_attention_backends_for_layers(model, gate_attn)
+    name = base_model if isinstance(base_model, str) else "custom"
+    return TokenGateModel(model, gate, int(gate_layer), name)

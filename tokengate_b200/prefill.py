@@ -1,0 +1,149 @@
+"""Batched gated prefill on the B200 kernels.
+
+Same control flow and return contract as the reference
+  prefill_batch_for_decode(model, gate, prompt_ids_list, article_starts,
+                           article_ends, gate_layer, K, prune_below_gate=False)
+  -> (first_tokens (B,1), cache, kept_positions (B, max_n_kept), n_kepts, K_clampeds)
+(tokengate/e2e_gate/gate_module/gate_forward.py:1269-1579):
+
+  Phase 1   layers 0..L on the right-padded full prompts, causal attention
+            (the tcgen05 kernel with no bias);
+  score     one gate_score launch over every request's state rows;
+  select    one topk_select launch: K_clamped = max(1, min(K, n_state)),
+            kept positions (prefix, sorted top-K, suffix) and the Phase-2 bias
+            row (score at kept state tokens, 0 elsewhere, -1e9 pads);
+  compact   one gather launch for the hidden rows (+ the below-gate K/V rows
+            of every layer <= L when prune_below_gate);
+  Phase 2   layers L+1..N-1 on the kept tokens with the key bias, RoPE at the
+            ORIGINAL positions;
+  head      final norm of each request's last kept row -> lm_head -> argmax.
+
+The reference's per-request Python loop for scoring/selection/gather and its
+host-side index construction are replaced by three batched launches; no host
+synchronisation happens between Phase 1 and the head.
+"""
+from typing import List, Optional, Sequence, Union
+
+import torch
+
+from . import ops
+from .gate import readout_vector
+from .model import PrefillCache, set_attn_scale_for_layers, set_gate_bias_for_layers
+
+# Phase-2 length bucket (the reference's set_phase2_bucket, gate_forward.py:531-546):
+# None = exact max_n_kept.
+_PHASE2_BUCKET: Optional[int] = None
+
+
+def set_phase2_bucket(n: Optional[int]) -> None:
+    global _PHASE2_BUCKET
+    _PHASE2_BUCKET = None if n is None else int(n)
+
+
+def _ids_to_device(prompt_ids_list, device) -> torch.Tensor:
+    B = len(prompt_ids_list)
+    if B == 1 and torch.is_tensor(prompt_ids_list[0]):
+        return prompt_ids_list[0].to(device=device, dtype=torch.long, non_blocking=True).reshape(1, -1)
+    lens = [len(x) for x in prompt_ids_list]
+    host = torch.zeros(B, max(lens), dtype=torch.long, pin_memory=torch.cuda.is_available())
+    for b, ids in enumerate(prompt_ids_list):
+        host[b, :lens[b]] = ids if torch.is_tensor(ids) else torch.as_tensor(ids, dtype=torch.long)
+    return host.to(device, non_blocking=True)
+
+
+@torch.no_grad()
+def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequence,
+                             article_starts: Sequence[int], article_ends: Sequence[int],
+                             gate_layer: int, K: Union[int, Sequence[int]],
+                             prune_below_gate: bool = False):
+    B = len(prompt_ids_list)
+    if B < 1:
+        raise ValueError("empty batch")
+    if len(article_starts) != B or len(article_ends) != B:
+        raise ValueError("one article start/end per prompt")
+    inner = model.model
+    n_layers = len(inner.layers)
+    if not 0 <= gate_layer < n_layers - 1:
+        raise ValueError(f"gate_layer {gate_layer} must leave at least one Phase-2 layer")
+    device = next(model.parameters()).device
+    lens = [int(x.numel()) if torch.is_tensor(x) else len(x) for x in prompt_ids_list]
+    starts = [int(s) for s in article_starts]
+    ends = [int(e) for e in article_ends]
+    for b in range(B):
+        if not 0 <= starts[b] < ends[b] <= lens[b]:
+            raise ValueError(f"request {b}: state span [{starts[b]}, {ends[b]}) invalid for length {lens[b]}")
+    max_seq_len = max(lens)
+
+    # ---- Phase 1
+    ids = _ids_to_device(prompt_ids_list, device)
+    set_gate_bias_for_layers(model, 0, gate_layer + 1, None)
+    hidden = inner.embed_tokens(ids)
+    position_ids = torch.arange(max_seq_len, device=device).unsqueeze(0).expand(B, -1)
+    pe = inner.rotary_emb(hidden, position_ids)
+    cache = PrefillCache(n_layers)
+    for i in range(gate_layer + 1):
+        hidden = inner.layers[i](hidden, attention_mask=None, position_ids=position_ids,
+                                 past_key_values=cache, use_cache=True, position_embeddings=pe)
+    del pe
+
+    # ---- score + select
+    w = readout_vector(gate, hidden.shape[-1], device)
+    n_state = [e - s for s, e in zip(starts, ends)]
+    scores = ops.gate_score(hidden, w, starts, n_state)
+    Ks = list(K) if isinstance(K, (list, tuple)) else [K] * B
+    K_clampeds = [max(1, min(int(Ks[b]), n_state[b])) for b in range(B)]
+    n_kepts = [starts[b] + K_clampeds[b] + (lens[b] - ends[b]) for b in range(B)]
+    max_n_kept = max(n_kepts)
+    n_alloc = max_n_kept if _PHASE2_BUCKET is None else -(-max_n_kept // _PHASE2_BUCKET) * _PHASE2_BUCKET
+    kept_positions, bias_row, _ = ops.topk_select(scores, n_state, K_clampeds, starts, lens,
+                                                  n_alloc, bias_dtype=hidden.dtype)
+
+    # ---- compact
+    H = hidden.shape[-1]
+    hs_pruned = torch.empty((B, n_alloc, H), dtype=hidden.dtype, device=device)
+    specs = [ops.gather_spec_rows(hidden, hs_pruned, 1)]
+    if prune_below_gate:
+        pruned_kv = []
+        for li in range(gate_layer + 1):
+            lc = cache.layers[li]
+            kd = lc.k_tok.new_empty((B, max_n_kept) + tuple(lc.k_tok.shape[2:]))
+            vd = lc.v_tok.new_empty((B, max_n_kept) + tuple(lc.v_tok.shape[2:]))
+            specs.append(ops.gather_spec_rows(lc.k_tok, kd, 1))
+            specs.append(ops.gather_spec_rows(lc.v_tok, vd, 1))
+            pruned_kv.append((kd, vd))
+    if prune_below_gate and max_n_kept != n_alloc:
+        # below-gate caches are max_n_kept wide (reference: pad to max_n_kept); one launch per width
+        ops.gather_rows(specs[:1], kept_positions, n_kepts, n_alloc, device)
+        ops.gather_rows(specs[1:], kept_positions, n_kepts, max_n_kept, device)
+    else:
+        ops.gather_rows(specs, kept_positions, n_kepts, n_alloc, device)
+    if prune_below_gate:
+        for li, (kd, vd) in enumerate(pruned_kv):
+            cache.layers[li].k_tok, cache.layers[li].v_tok = kd, vd
+    del hidden, scores
+
+    # ---- Phase 2
+    # The reference hands the bf16 bias to every layer and each converts it to
+    # fp32 (_bias_bhs); converting once here gives the same values.
+    gate_bias = bias_row.float()
+    set_gate_bias_for_layers(model, gate_layer + 1, n_layers, gate_bias, per_head=False)
+    attn_scale = None
+    if hasattr(gate, "attn_scale_eff") and not getattr(gate, "_baseline_no_bias_scale", False):
+        attn_scale = gate.attn_scale_eff()
+    set_attn_scale_for_layers(model, gate_layer + 1, n_layers, attn_scale)
+    pe2 = inner.rotary_emb(hs_pruned, kept_positions)
+    for i in range(gate_layer + 1, n_layers):
+        hs_pruned = inner.layers[i](hs_pruned, attention_mask=None, position_ids=kept_positions,
+                                    past_key_values=cache, use_cache=True, position_embeddings=pe2)
+
+    # ---- head
+    last_valid = torch.tensor([n - 1 for n in n_kepts], device=device)
+    hs_last = inner.norm(hs_pruned[torch.arange(B, device=device), last_valid])
+    first_tokens = model.lm_head(hs_last).argmax(-1, keepdim=True)
+    if n_alloc != max_n_kept:
+        for i in range(gate_layer + 1, n_layers):
+            lc = cache.layers[i]
+            lc.k_tok = lc.k_tok[:, :max_n_kept]
+            lc.v_tok = lc.v_tok[:, :max_n_kept]
+        kept_positions = kept_positions[:, :max_n_kept]
+    return first_tokens, cache, kept_positions, n_kepts, K_clampeds
