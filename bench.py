@@ -242,6 +242,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="after the warm-up, run ONE step between cudaProfilerStart/Stop and exit "
+                         "(for ncu --profile-from-start off); prints no bench line")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -296,6 +299,14 @@ def main():
     for _ in range(args.warmup):
         step_device()
     barrier()
+    if args.profile_step:
+        torch.cuda.profiler.start()
+        step_device()
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
+        if pg is not None:
+            pg.destroy_process_group()
+        return 0
     clocks = ClockSampler(local) if rank == 0 else None
     if clocks:
         clocks.start()

@@ -1,0 +1,89 @@
+"""Single-kernel runs of the four hot-path kernels at BASELINE shapes (timing and ncu captures).
+
+    python -m tokengate_b200.microbench attn   [--seq 32768] [--batch 1] [--hq 16] [--hkv 8] [--iters 20]
+    python -m tokengate_b200.microbench score  [--seq 32768] [--batch 1] [--iters 20]
+    python -m tokengate_b200.microbench topk   [--k 2000] [--batch 1] [--iters 20]
+    python -m tokengate_b200.microbench gather [--k 2000] [--batch 1] [--iters 20]
+
+Prints one JSON line per run with the CUDA-event time per launch and the
+algorithmic FLOPs or bytes of one launch (attention: 4*B*Hq*D*S(S+1)/2;
+score: the bf16 state rows + w + fp32 scores; topk: scores read + keep/bias
+written; gather: hidden rows + 4 below-gate K/V tensors read and written).
+"""
+import argparse
+import json
+
+import torch
+
+from . import ops
+
+
+def _time(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel", choices=("attn", "score", "topk", "gather"))
+    ap.add_argument("--seq", type=int, default=32768)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--hq", type=int, default=16)
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--hidden", type=int, default=2048)
+    ap.add_argument("--k", type=int, default=2000)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--no-bias", action="store_true")
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    B, S = a.batch, a.seq
+    res = dict(kernel=a.kernel, batch=B)
+    if a.kernel == "attn":
+        q = torch.randn(B, S, a.hq, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        k = torch.randn(B, S, a.hkv, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        v = torch.randn(B, S, a.hkv, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        bias = None if a.no_bias else torch.randn(B, 1, S, device=dev, generator=g)
+        ms = _time(lambda: ops.keybias_attention(q, k, v, bias=bias), a.iters)
+        flops = 4.0 * B * a.hq * 128 * S * (S + 1) / 2
+        res.update(seq=S, hq=a.hq, hkv=a.hkv, bias=not a.no_bias, ms=ms, tflop=flops / 1e12,
+                   tflops=flops / ms / 1e9)
+    else:
+        st0, st1 = 512, S - 256
+        n_art = st1 - st0
+        h = torch.randn(B, S, a.hidden, device=dev, dtype=torch.bfloat16, generator=g)
+        w = torch.randn(a.hidden, device=dev, generator=g) / a.hidden ** 0.5
+        sc = ops.gate_score(h, w, [st0] * B, [n_art] * B)
+        n_kept = st0 + a.k + (S - st1)
+        if a.kernel == "score":
+            ms = _time(lambda: ops.gate_score(h, w, [st0] * B, [n_art] * B, out=sc), a.iters)
+            byts = B * (n_art * a.hidden * 2 + n_art * 4) + a.hidden * 4
+        elif a.kernel == "topk":
+            keep = torch.empty(B, n_kept, dtype=torch.int64, device=dev)
+            bias = torch.empty(B, n_kept, dtype=torch.bfloat16, device=dev)
+            ms = _time(lambda: ops.topk_select(sc, [n_art] * B, [a.k] * B, [st0] * B, [S] * B, n_kept,
+                                               keep_out=keep, bias_out=bias), a.iters)
+            byts = B * (n_art * 4 + n_kept * 10)
+        else:
+            keep, _, _ = ops.topk_select(sc, [n_art] * B, [a.k] * B, [st0] * B, [S] * B, n_kept)
+            kv = [torch.randn(B, S, a.hkv, 128, device=dev, dtype=torch.bfloat16, generator=g) for _ in range(4)]
+            dh = torch.empty(B, n_kept, a.hidden, device=dev, dtype=torch.bfloat16)
+            dkv = [torch.empty(B, n_kept, a.hkv, 128, device=dev, dtype=torch.bfloat16) for _ in range(4)]
+            specs = [ops.gather_spec_rows(h, dh, 1)] + [ops.gather_spec_rows(s, d, 1) for s, d in zip(kv, dkv)]
+            ms = _time(lambda: ops.gather_rows(specs, keep, [n_kept] * B, n_kept, dev), a.iters)
+            byts = B * 2 * n_kept * (a.hidden * 2 + 4 * a.hkv * 128 * 2) + B * n_kept * 8
+        res.update(seq=S, k=a.k, ms=ms, us=ms * 1e3, mbytes=byts / 1e6, gbs=byts / ms / 1e6)
+    assert ops.device_error() == 0
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()
