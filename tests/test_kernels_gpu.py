@@ -49,12 +49,15 @@ def _check_attn(q, k, v, bias_bhs, causal, rows=None, qrs=None, scale=None):
     bb = None
     if bias_bhs is not None:
         bb = torch.broadcast_to(bias_bhs.detach().cpu(), (B, Hq, Sk)).numpy()
-    qs = None
+    qref = q.float().cpu()
     if qrs is not None:
-        qs = torch.broadcast_to(qrs.detach().cpu(), (B, Hq, Sq)).numpy()
-    ref, ref_lse = oatt.keybias_attention(q.float().cpu().numpy(), k.float().cpu().numpy(),
+        # the reference scales q by the row scale in bf16 before attention
+        # (qwen3_flex_attention.py:447-451); the kernel does the same
+        qs = torch.broadcast_to(qrs.detach().cpu(), (B, Hq, Sq)).permute(0, 2, 1).unsqueeze(-1)
+        qref = (qref * qs).to(torch.bfloat16).float()
+    ref, ref_lse = oatt.keybias_attention(qref.numpy(), k.float().cpu().numpy(),
                                           v.float().cpu().numpy(), bb, scale=scale, causal=causal,
-                                          rows=rows, q_row_scale=qs)
+                                          rows=rows)
     got = out.float().cpu().numpy()[:, rows]
     err = np.abs(got - ref).max()
     cos = _cos(got, ref)

@@ -8,18 +8,25 @@
 //  * one CTA owns TWO 128-row query tiles that share one KV head: two heads
 //    of a GQA group at the same rows (Hq/Hkv even), or two consecutive row
 //    blocks of one head otherwise. K/V tiles are loaded once for both.
+//  * the key bias rides in the QK product: each K tile gets a 16-column
+//    extension [b0_hi, b0_lo, b1_hi, b1_lo, 0...] (bias / scale split into two
+//    bf16 that sum to it to ~16 bits) and each Q tile a constant one-hot
+//    extension selecting its head's pair, so one extra K=16 MMA step adds
+//    the bias in fp32 and the softmax never touches it;
 //  * warp 8 streams Q/K/V through TMA (128-byte swizzle, no multicast) into a
-//    2-stage ring and stages the bias of each key block (pre-multiplied by
-//    log2 e, -inf past Sk) next to the V tile;
-//  * warp 9 issues tcgen05.mma (M=128, N=128, K=16 steps): S_t = Q_t K^T into
-//    TMEM, then O_t += P_t V with P read straight from TMEM (it overwrites
-//    the first 64 columns of S_t as packed bf16 pairs);
+//    2-stage ring and writes each K stage's bias extension (32-byte swizzle)
+//    from the fp32 bias in global memory;
+//  * warp 9 issues tcgen05.mma (M=128, N=128, K=16 steps): S_t = Q_t K^T
+//    (+ bias step) into TMEM, then O_t += P_t V with P read straight from
+//    TMEM (it overwrites the first 64 columns of S_t as packed bf16 pairs);
 //  * warps 0-3 / 4-7 are the softmax warpgroups of tile 0 / tile 1: one TMEM
-//    lane (= one query row) per thread, the whole 128-key row in registers,
-//    x = S*scale*log2e + bias*log2e in one FFMA, exp2 on the MUFU. The running
-//    max is only moved (and O rescaled in TMEM) when it grows by more than
-//    2^8, so rescales are rare; numerator and denominator share the stale max,
-//    so the result is exact.
+//    lane (= one query row) per thread, the 128-key row in registers, a
+//    3-input max over the raw logits, p = 2^(S*scale*log2e - m) with one
+//    packed FFMA2 per pair, exp2 on the MUFU for three of every four pairs
+//    and on the FMA pipe (polynomial) for the fourth. The running max is only
+//    moved (and O rescaled in TMEM) when it grows by more than 2^8, so
+//    rescales are rare; numerator and denominator share the stale max, so
+//    the result is exact.
 //  * TMEM: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512) columns.
 //
 // Issue order of the MMA warp per key block j (tile 0, tile 1):
@@ -36,17 +43,21 @@ namespace tg {
 constexpr int kAttnBM = 128;
 constexpr int kAttnBN = 128;
 constexpr int kAttnD = 128;
-constexpr int kAttnThreads = 320;
+constexpr int kAttnThreads = 384;  // 3 warpgroups: softmax 0, softmax 1, producer/MMA
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr int kAttnTileBytes = kAttnBM * kAttnD * 2;  // 32 KB: one Q/K/V tile
 constexpr int kAttnHalfBytes = kAttnTileBytes / 2;    // 16 KB: 64 columns (one TMA box)
+constexpr int kExtBytes = 128 * 32;                   // 4 KB: 128 rows x 16 bf16 extension
 
 // dynamic shared memory layout (offsets from a 1024-byte aligned base)
 constexpr int kSmQ = 0;                                  // 2 tiles
 constexpr int kSmK = kSmQ + 2 * kAttnTileBytes;          // 2 stages
 constexpr int kSmV = kSmK + 2 * kAttnTileBytes;          // 2 stages
-constexpr int kSmBias = kSmV + 2 * kAttnTileBytes;       // [stage][tile][128] fp32
-constexpr int kSmBar = kSmBias + 2 * 2 * kAttnBN * 4;
-constexpr int kNumBars = 16;
+constexpr int kSmKExt = kSmV + 2 * kAttnTileBytes;       // 2 stages: K bias extension
+constexpr int kSmQExt = kSmKExt + 2 * kExtBytes;         // 2 tiles: Q one-hot extension
+constexpr int kSmBar = kSmQExt + 2 * kExtBytes;
+constexpr int kNumBars = 17;
 constexpr int kSmTmemSlot = kSmBar + kNumBars * 8;
 constexpr int kAttnSmemBytes = kSmTmemSlot + 16 + 1024;  // + alignment slack
 
@@ -60,7 +71,8 @@ enum {
   BAR_S_FULL = 9,   // 2 (per tile)
   BAR_P_FULL = 11,  // 2 (per tile)
   BAR_O_FULL = 13,  // 2 (per tile)
-  BAR_MMA_DONE = 15
+  BAR_MMA_DONE = 15,
+  BAR_Q_READY = 16  // softmax warps scaled their Q rows (only with a row scale)
 };
 
 // device error bits
@@ -74,6 +86,7 @@ enum : unsigned int {
   ERR_ATTN_S_FULL = 1u << 6,
   ERR_ATTN_O_FULL = 1u << 7,
   ERR_ATTN_DRAIN = 1u << 8,
+  ERR_ATTN_Q_READY = 1u << 9,
 };
 
 struct AttnParams {
@@ -91,6 +104,7 @@ struct AttnParams {
   int n_mblocks;   // ceil(Sq / 128)
   int n_kblocks;   // ceil(Sk / 128)
   int heads_per_unit_row;  // pair_heads ? Hq/2 : Hq
+  float scale;             // softmax_scale
   float scale_log2;        // softmax_scale * log2(e)
   unsigned int* err;
 };
@@ -140,6 +154,25 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, unsigne
   return __all_sync(0xffffffffu, ok);
 }
 
+// byte offset of 16-byte chunk c (0/1) of row r in a 32-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw32_off(int r, int c) {
+  return (uint32_t)r * 32u + ((uint32_t)(c ^ ((r >> 2) & 1)) << 4);
+}
+
+// byte offset of 16-byte chunk c (0..7) of row r in one 128-byte-swizzled
+// 64-column half of a Q/K/V tile
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+  return (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
+}
+
+// (hi, lo) bf16 pair whose sum is v to ~16 bits; -inf -> (-inf, 0)
+__device__ __forceinline__ uint32_t split_bf16x2(float v) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+  const float hf = __bfloat162float(hi);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(isfinite(hf) ? v - hf : 0.f);
+  return (uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(lo) << 16);
+}
+
 __global__ void __launch_bounds__(kAttnThreads, 1)
     keybias_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k,
@@ -149,7 +182,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                              ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sQ = sbase + kSmQ, sK = sbase + kSmK, sV = sbase + kSmV;
-  float* sBias = reinterpret_cast<float*>(smem + kSmBias);
+  const uint32_t sKExt = sbase + kSmKExt, sQExt = sbase + kSmQExt;
   const uint32_t sBar = sbase + kSmBar;
   auto bar = [&](int i) { return sBar + 8u * i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmTmemSlot);
@@ -157,6 +190,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.y;
+  const bool has_bias = p.bias != nullptr;
+  const bool has_qscale = p.qscale != nullptr;
 
   TileInfo ti[2];
   attn_unit(p, ti);
@@ -175,9 +210,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(bar(BAR_O_FULL + s), 1);
     }
     mbar_init(bar(BAR_MMA_DONE), 1);
+    mbar_init(bar(BAR_Q_READY), 8);
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (has_bias && threadIdx.x < 256) {
+    // Q extension: row r of tile t holds ones in the columns of its head's
+    // (hi, lo) pair: (2t, 2t+1) for a head pair, (0, 1) for two row blocks.
+    // K extension: chunk 1 (columns 8..15) is zero in both stages; chunk 0
+    // is rewritten per key block by the producer.
+    const int t = threadIdx.x >> 7, r = threadIdx.x & 127;
+    const int col = p.pair_heads ? 2 * t : 0;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    w[col >> 1] = 0x3F803F80u;  // two bf16 ones
+    uint8_t* qe = smem + kSmQExt + t * kExtBytes;
+    *reinterpret_cast<uint4*>(qe + sw32_off(r, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(qe + sw32_off(r, 1)) = make_uint4(0u, 0u, 0u, 0u);
+    uint8_t* ke = smem + kSmKExt + t * kExtBytes;  // t doubles as the stage here
+    *reinterpret_cast<uint4*>(ke + sw32_off(r, 1)) = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
+  }
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -186,7 +238,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  // Register split (launch: 384 threads x 168 = 64512): the two softmax
+  // warpgroups take 224 each, the producer/MMA warpgroup keeps 56:
+  // 2*128*224 + 128*56 = 64512. Each role's code is dominated by its own
+  // setmaxnreg so the allocator gives it that budget.
+  if (warp >= kProducerWarp) {
+  setmaxnreg_dec<56>();
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -201,12 +259,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tma_load_4d(dst + kAttnHalfBytes, &tm_q, bar(BAR_Q), 64, ti[t].head, ti[t].m0, b);
       }
     }
-    const float kLog2e = 1.4426950408889634f;
+    const float inv_scale = 1.f / p.scale;
+    const float* brow0 = has_bias ? p.bias + (int64_t)b * p.bias_sb + (int64_t)ti[0].head * p.bias_sh : nullptr;
+    const float* brow1 = has_bias ? p.bias + (int64_t)b * p.bias_sb + (int64_t)ti[1].head * p.bias_sh : nullptr;
     int issued = 0;
     for (int j = 0; j < nblk; ++j) {
       const int s = j & 1;
       const uint32_t ph = (j >> 1) & 1;
+      // this lane's four key rows of block j: bias of both tiles' heads
+      float bv0[4], bv1[4];
+      if (has_bias) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int key = j * kAttnBN + lane + 32 * u;
+          bv0[u] = key < p.Sk ? __ldg(brow0 + key) : 0.f;
+          bv1[u] = key < p.Sk ? __ldg(brow1 + key) : 0.f;
+        }
+      }
       if (!warp_wait(bar(BAR_K_EMPTY + s), ph ^ 1, p.err, ERR_ATTN_K_EMPTY)) break;
+      if (has_bias) {
+        uint8_t* ke = smem + kSmKExt + s * kExtBytes;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int r = lane + 32 * u;
+          const uint32_t w0 = split_bf16x2(bv0[u] * inv_scale);
+          const uint32_t w1 = p.pair_heads ? split_bf16x2(bv1[u] * inv_scale) : 0u;
+          *reinterpret_cast<uint4*>(ke + sw32_off(r, 0)) = make_uint4(w0, w1, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
       if (lane == 0) {
         const uint32_t dst = sK + s * kAttnTileBytes;
         mbar_arrive_expect_tx(bar(BAR_K_FULL + s), kAttnTileBytes);
@@ -217,25 +299,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         issued = 2 * j + 1;
         break;
       }
-      // bias of key block j for both tiles, in log2 units; -inf past Sk
-      float* bdst = sBias + s * 2 * kAttnBN;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int e = lane + 32 * i;
-        const int t = e >> 7, c = e & 127;
-        const int key = j * kAttnBN + c;
-        float val;
-        if (key >= p.Sk) {
-          val = -INFINITY;
-        } else if (p.bias != nullptr) {
-          const int hh = t ? ti[1].head : ti[0].head;
-          val = __ldg(p.bias + (int64_t)b * p.bias_sb + (int64_t)hh * p.bias_sh + key) * kLog2e;
-        } else {
-          val = 0.f;
-        }
-        bdst[e] = val;
-      }
-      __syncwarp();
       if (lane == 0) {
         const uint32_t dst = sV + s * kAttnTileBytes;
         mbar_arrive_expect_tx(bar(BAR_V_FULL + s), kAttnTileBytes);
@@ -257,7 +320,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (lastv >= 0) mbar_wait(bar(BAR_V_FULL + s), (lastv >> 1) & 1, p.err, ERR_ATTN_DRAIN);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdescQK = umma_idesc_bf16(128, 128, 0, 0);
@@ -268,9 +331,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kAttnHalfBytes + (kk & 3) * 32;
           umma_ss(tmem + t * 128u, umma_desc_sw128(qa + off, 16, 1024),
-                  umma_desc_sw128(ka + off, 16, 1024),
-                  kIdescQK, kk > 0);
+                  umma_desc_sw128(ka + off, 16, 1024), kIdescQK, kk > 0);
         }
+        if (has_bias)
+          umma_ss(tmem + t * 128u, umma_desc_sw32(sQExt + t * kExtBytes, 16, 256),
+                  umma_desc_sw32(sKExt + s * kExtBytes, 16, 256), kIdescQK, 1u);
       };
       auto issue_pv = [&](int t, int s, bool acc) {
         const uint32_t va = sV + s * kAttnTileBytes;
@@ -282,6 +347,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       };
       bool ok = mbar_wait(bar(BAR_Q), 0, p.err, ERR_ATTN_Q);
+      if (ok && has_qscale) ok = mbar_wait(bar(BAR_Q_READY), 0, p.err, ERR_ATTN_Q_READY);
       if (ok && nblk > 0) ok = mbar_wait(bar(BAR_K_FULL + 0), 0, p.err, ERR_ATTN_K_FULL);
       if (ok && nblk > 0) {
         tc_fence_after();
@@ -332,7 +398,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_wait(bar(BAR_MMA_DONE), 0, p.err, ERR_ATTN_DRAIN);
     }
     __syncwarp();
+  }
   } else {
+    setmaxnreg_inc<224>();
     // ------------------------------------------------------------ softmax
     const int t = warp >> 2;
     const int sub = warp & 3;
@@ -342,48 +410,69 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const uint32_t tS = tmem + t * 128u + lane_off;
     const uint32_t tO = tmem + 256u + t * 128u + lane_off;
-
-    float rowscale = p.scale_log2;
-    if (p.qscale != nullptr && i < p.Sq)
-      rowscale *= __ldg(p.qscale + (int64_t)b * p.qs_sb + (int64_t)me.head * p.qs_sh + i);
-
-    float m_run = -INFINITY;
-    float l_run = 0.f;
     bool ok = true;
-    const int diag_blk = p.causal ? (me.m0 / kAttnBN) : -1;
 
-    for (int j = 0; j < me.nblk; ++j) {
-      const int s = j & 1;
+    if (has_qscale) {
+      // the Phase-2 query scale: q_row <- bf16(q_row * qs), in shared memory
+      // before the first QK MMA (the reference scales q the same way)
+      ok = warp_wait(bar(BAR_Q), 0, p.err, ERR_ATTN_Q);
+      if (ok && me.nblk > 0) {
+        const float qs = (i < p.Sq)
+            ? __ldg(p.qscale + (int64_t)b * p.qs_sb + (int64_t)me.head * p.qs_sh + i) : 1.f;
+        uint8_t* qt = smem + kSmQ + t * kAttnTileBytes;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4* ptr = reinterpret_cast<uint4*>(qt + hh * kAttnHalfBytes + sw128_off(r, c));
+            uint4 v = *ptr;
+            uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float lo = __uint_as_float(w[e] << 16) * qs;
+              const float hi = __uint_as_float(w[e] & 0xFFFF0000u) * qs;
+              w[e] = pack_bf16x2(lo, hi);
+            }
+            *ptr = v;
+          }
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_Q_READY));
+    }
+
+    const float c2 = p.scale_log2;   // raw logit -> log2 units
+    const float2 c22 = make_float2(c2, c2);
+    float m_run = -INFINITY;         // running max, log2 units
+    float l_run = 0.f;
+    const int diag_blk = p.causal ? (me.m0 / kAttnBN) : -1;
+    const int last_blk = me.nblk - 1;
+    const int tail_keys = p.Sk - last_blk * kAttnBN;  // valid keys in the last block
+
+    for (int j = 0; ok && j < me.nblk; ++j) {
       if (!warp_wait(bar(BAR_S_FULL + t), j & 1, p.err, ERR_ATTN_S_FULL)) { ok = false; break; }
-      if (!warp_wait(bar(BAR_V_FULL + s), (j >> 1) & 1, p.err, ERR_ATTN_V_FULL)) { ok = false; break; }
       tc_fence_after();
 
       uint32_t sv[128];
       tmem_ld128(tS, sv);
 
-      const float4* bj = reinterpret_cast<const float4*>(sBias + (s * 2 + t) * kAttnBN);
-      float mx = -INFINITY;
-      const bool diag = (j == diag_blk);
+      // masks: causal edge (keys past the query row) and keys past Sk
+      if (j == diag_blk || (!p.causal && j == last_blk && tail_keys < kAttnBN)) {
+        const int lim = (j == diag_blk) ? r : tail_keys - 1;
 #pragma unroll
-      for (int c4 = 0; c4 < 32; ++c4) {
-        const float4 bb = bj[c4];
-        float x0 = fmaf(__uint_as_float(sv[4 * c4 + 0]), rowscale, bb.x);
-        float x1 = fmaf(__uint_as_float(sv[4 * c4 + 1]), rowscale, bb.y);
-        float x2 = fmaf(__uint_as_float(sv[4 * c4 + 2]), rowscale, bb.z);
-        float x3 = fmaf(__uint_as_float(sv[4 * c4 + 3]), rowscale, bb.w);
-        if (diag) {
-          const int c = 4 * c4;
-          if (c + 0 > r) x0 = -INFINITY;
-          if (c + 1 > r) x1 = -INFINITY;
-          if (c + 2 > r) x2 = -INFINITY;
-          if (c + 3 > r) x3 = -INFINITY;
-        }
-        sv[4 * c4 + 0] = __float_as_uint(x0);
-        sv[4 * c4 + 1] = __float_as_uint(x1);
-        sv[4 * c4 + 2] = __float_as_uint(x2);
-        sv[4 * c4 + 3] = __float_as_uint(x3);
-        mx = fmaxf(mx, fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)));
+        for (int c = 0; c < 128; ++c)
+          if (c > lim) sv[c] = __float_as_uint(-INFINITY);
       }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; c += 8) {
+        mx0 = fmax3(mx0, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
+        mx1 = fmax3(mx1, __uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]));
+        mx2 = fmax3(mx2, __uint_as_float(sv[c + 4]), __uint_as_float(sv[c + 5]));
+        mx3 = fmax3(mx3, __uint_as_float(sv[c + 6]), __uint_as_float(sv[c + 7]));
+      }
+      const float mx = fmax3(fmaxf(mx0, mx1), mx2, mx3) * c2;
 
       // lazy max: move it (and rescale O) only when it grows by more than 8 in
       // log2 units; O is stable here because S_t(j) completing implies the
@@ -400,17 +489,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m_run = m_new;
       }
       const float msub = (m_run == -INFINITY) ? 0.f : m_run;
-      uint32_t pk[64];
-      float lsum = 0.f;
+      const float2 negm = make_float2(-msub, -msub);
+
+      // p = 2^(S*c2 - m): one FFMA2 per pair; three of every four pairs on
+      // the MUFU, one on the FMA pipe; packed bf16 pairs in two halves
+      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2_approx(__uint_as_float(sv[2 * c]) - msub);
-        const float p1 = ex2_approx(__uint_as_float(sv[2 * c + 1]) - msub);
-        lsum += p0 + p1;
-        pk[c] = pack_bf16x2(p0, p1);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const int c = half * 64 + 2 * q;
+          const float2 d = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
+                                      c22, negm);
+          float2 pp;
+          if ((q & 3) == 3) {
+            pp = exp2_poly2(d);
+          } else {
+            pp.x = ex2_approx(d.x);
+            pp.y = ex2_approx(d.y);
+          }
+          if (q & 1) ls1 = __fadd2_rn(ls1, pp); else ls0 = __fadd2_rn(ls0, pp);
+          pk[q] = pack_bf16x2(pp.x, pp.y);
+        }
+        tmem_st32(tS + half * 32, pk);
       }
-      l_run += lsum;
-      tmem_st64(tS, pk);
+      l_run += (ls0.x + ls0.y) + (ls1.x + ls1.y);
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -460,7 +564,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

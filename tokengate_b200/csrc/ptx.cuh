@@ -71,6 +71,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
   }
 }
 
+// Warpgroup-wide register budget changes (all 128 threads of the warpgroup
+// must execute them; the sum over warpgroups must fit the launch budget).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// bar.sync on a named barrier (1..15) for `count` threads (whole warps).
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -149,6 +165,23 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// UMMA shared-memory descriptor, 32-byte swizzle (layout type 6), version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw32(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)6 << 61;  // SWIZZLE_32B
+  return d;
+}
+
+// Orders this thread's prior generic-proxy shared-memory writes before later
+// async-proxy (TMA / tensor core) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Instruction descriptor for kind::f16 with bf16 inputs and fp32 accumulate.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n, int a_mn_major,
                                                        int b_mn_major) {
@@ -207,6 +240,33 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two values on the FMA pipe: x clamped to [-120, 64], rounded to
+// n + f with |f| <= 1/2 by the 1.5*2^23 shifter, 2^f from a degree-3
+// polynomial fitted (relative minimax, 7.5e-5) on [-1/2, 1/2], and n added
+// to the exponent field. For inputs below -120 it returns 2^-120, not 0.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fminf(fmaxf(x.x, -120.f), 64.f);
+  x.y = fminf(fmaxf(x.y, -120.f), 64.f);
+  const float2 shifter = make_float2(12582912.f, 12582912.f);
+  const float2 t = __fadd2_rn(x, shifter);
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  float2 q = __ffma2_rn(make_float2(0.05517097935f, 0.05517097935f), f,
+                        make_float2(0.24260970950f, 0.24260970950f));
+  q = __ffma2_rn(q, f, make_float2(0.69326096773f, 0.69326096773f));
+  q = __ffma2_rn(q, f, make_float2(0.99992817640f, 0.99992817640f));
+  float2 r;
+  r.x = __int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23));
+  r.y = __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23));
+  return r;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

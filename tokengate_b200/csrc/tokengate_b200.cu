@@ -193,6 +193,7 @@ int tg_keybias_attn_fwd(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
   p.n_mblocks = (Sq + tg::kAttnBM - 1) / tg::kAttnBM;
   p.n_kblocks = (Sk + tg::kAttnBN - 1) / tg::kAttnBN;
   p.heads_per_unit_row = p.pair_heads ? Hq / 2 : Hq;
+  p.scale = softmax_scale;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   if ((st = device_error_ptr(&p.err))) return st;
 
