@@ -113,15 +113,39 @@ __global__ void __launch_bounds__(256) gate_score_kernel(const ScoreParams p) {
     wr[i][4] = c.x; wr[i][5] = c.y; wr[i][6] = c.z; wr[i][7] = c.w;
   }
 
-  int req = 0;
-  for (int64_t g = warp_global; g < p.total_rows; g += n_warps) {
-    while (g >= p.row_off[req + 1]) ++req;  // rows are visited in increasing order
-    const int64_t r = g - p.row_off[req];
-    const __nv_bfloat16* row = p.h + (int64_t)req * p.h_sb + (int64_t)(p.begin[req] + r) * p.h_ss;
-    uint4 hv[NV];
+  // rows are visited in increasing order by each warp; `req` tracks the
+  // request of the row, the next row's 16-byte vectors are loaded before the
+  // current row is reduced
+  int req = 0, nreq = 0;
+  auto row_ptr = [&](int64_t g, int& rq) {
+    while (g >= p.row_off[rq + 1]) ++rq;
+    const int64_t r = g - p.row_off[rq];
+    return p.h + (int64_t)rq * p.h_sb + (int64_t)(p.begin[rq] + r) * p.h_ss;
+  };
+  constexpr bool kPrefetch = NV <= 8;  // wider rows would spill the second buffer
+  uint4 hv[NV], hn[kPrefetch ? NV : 1];
+  int64_t g = warp_global;
+  if (kPrefetch && g < p.total_rows) {
+    const __nv_bfloat16* row = row_ptr(g, nreq);
 #pragma unroll
-    for (int i = 0; i < NV; ++i)
-      hv[i] = ld_nc_v4(reinterpret_cast<const uint4*>(row + 8 * (lane + 32 * i)));
+    for (int i = 0; i < NV; ++i) hn[i] = ld_nc_v4(reinterpret_cast<const uint4*>(row + 8 * (lane + 32 * i)));
+  }
+  for (; g < p.total_rows; g += n_warps) {
+    if constexpr (kPrefetch) {
+      req = nreq;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) hv[i] = hn[i];
+      const int64_t gn = g + n_warps;
+      if (gn < p.total_rows) {
+        const __nv_bfloat16* row = row_ptr(gn, nreq);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) hn[i] = ld_nc_v4(reinterpret_cast<const uint4*>(row + 8 * (lane + 32 * i)));
+      }
+    } else {
+      const __nv_bfloat16* row = row_ptr(g, req);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) hv[i] = ld_nc_v4(reinterpret_cast<const uint4*>(row + 8 * (lane + 32 * i)));
+    }
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
@@ -137,7 +161,7 @@ __global__ void __launch_bounds__(256) gate_score_kernel(const ScoreParams p) {
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1)
       acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
-    if (lane == 0) p.out[(int64_t)req * p.out_sb + r] = tg_logsigmoid(acc);
+    if (lane == 0) p.out[(int64_t)req * p.out_sb + (g - p.row_off[req])] = tg_logsigmoid(acc);
   }
 }
 

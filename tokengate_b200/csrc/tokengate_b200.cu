@@ -257,18 +257,29 @@ int tg_gate_score(const void* hidden, int64_t h_sb, int64_t h_ss, int hidden_dim
     }
     p.total_rows = p.row_off[nb];
     if (p.total_rows == 0) continue;
-    const int64_t warps_needed = p.total_rows;
-    int64_t blocks = (warps_needed + 7) / 8;
-    if (blocks > 148 * 16) blocks = 148 * 16;
-    switch (nv) {
-      case 1: tg::gate_score_kernel<1><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-      case 2: tg::gate_score_kernel<2><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-      case 4: tg::gate_score_kernel<4><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-      case 8: tg::gate_score_kernel<8><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-      case 10: tg::gate_score_kernel<10><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-      case 16: tg::gate_score_kernel<16><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-      default: tg::gate_score_kernel<20><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+    // resident grid: every warp streams many rows (prefetching the next)
+    int sms = 148;
+    {
+      int dev = 0;
+      if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     }
+    void (*kern)(const tg::ScoreParams) = nullptr;
+    switch (nv) {
+      case 1: kern = tg::gate_score_kernel<1>; break;
+      case 2: kern = tg::gate_score_kernel<2>; break;
+      case 4: kern = tg::gate_score_kernel<4>; break;
+      case 8: kern = tg::gate_score_kernel<8>; break;
+      case 10: kern = tg::gate_score_kernel<10>; break;
+      case 16: kern = tg::gate_score_kernel<16>; break;
+      default: kern = tg::gate_score_kernel<20>; break;
+    }
+    int per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    int64_t blocks = (p.total_rows + 7) / 8;
+    if (blocks > (int64_t)sms * per_sm) blocks = (int64_t)sms * per_sm;
+    kern<<<(unsigned)blocks, 256, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gate score launch");
   }
@@ -319,7 +330,14 @@ int tg_topk_select(const float* scores, int64_t s_sb, int B, const int32_t* n_st
       p.begin[i] = state_begin[b0 + i];
       p.seq_len[i] = seq_len[b0 + i];
     }
-    tg::topk_select_kernel<<<nb, tg::kTopkThreads, 0, s>>>(p);
+    int n_max = 0;
+    for (int i = 0; i < nb; ++i) n_max = p.n_state[i] > n_max ? p.n_state[i] : n_max;
+    if (n_max <= tg::kTopkThreads * 8)
+      tg::topk_select_reg_kernel<8><<<nb, tg::kTopkThreads, 0, s>>>(p);
+    else if (n_max <= tg::kTopkThreads * tg::kTopkRegKeys)
+      tg::topk_select_reg_kernel<tg::kTopkRegKeys><<<nb, tg::kTopkThreads, 0, s>>>(p);
+    else
+      tg::topk_select_kernel<<<nb, tg::kTopkThreads, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "top-k launch");
   }
@@ -367,9 +385,15 @@ int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t
                     n_valid[b0 + i], n_rows);
       p.n_valid[i] = n_valid[b0 + i];
     }
+    int sms = 148;
+    {
+      int dev = 0;
+      if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
     const int64_t warps = (int64_t)nb * n_tensors * n_rows;
     int64_t blocks = (warps + 7) / 8;
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;  // two resident waves, grid-stride rows
     tg::gather_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gather launch");

@@ -23,6 +23,7 @@ namespace tg {
 
 constexpr int kTopkMaxReq = 64;
 constexpr int kTopkThreads = 1024;
+constexpr int kTopkRegKeys = 32;  // keys per thread held in registers (n_state <= 32768)
 
 struct TopkParams {
   const float* scores;
@@ -44,6 +45,11 @@ struct TopkParams {
 __device__ __forceinline__ uint32_t order_key(float x) {
   const uint32_t u = __float_as_uint(x);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// inverse of order_key
+__device__ __forceinline__ float key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
 // exclusive block scan of one value per thread (kTopkThreads threads)
@@ -82,6 +88,11 @@ __device__ __forceinline__ void store_bias(const TopkParams& p, int b, int q, fl
     reinterpret_cast<__nv_bfloat16*>(p.bias_out)[(int64_t)b * p.bias_sb + q] = __float2bfloat16_rn(v);
 }
 
+__device__ __forceinline__ void topk_write_fixed(const TopkParams& p, int b, int begin, int K,
+                                                 int end, int n_kept, int64_t* keep);
+
+// Large requests (n_state > kTopkThreads * kTopkRegKeys): keys are re-read
+// from global memory (L1/L2 resident) in every pass.
 __global__ void __launch_bounds__(kTopkThreads, 1) topk_select_kernel(const TopkParams p) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s_warp[32];
@@ -186,7 +197,14 @@ __global__ void __launch_bounds__(kTopkThreads, 1) topk_select_kernel(const Topk
   }
 
   // ---- prefix, suffix and padding slots
-  for (int q = tid; q < p.n_alloc; q += kTopkThreads) {
+  topk_write_fixed(p, b, begin, K, end, n_kept, keep);
+}
+
+// Prefix, suffix and padding slots of the kept list (everything but the
+// selected state tokens).
+__device__ __forceinline__ void topk_write_fixed(const TopkParams& p, int b, int begin, int K,
+                                                 int end, int n_kept, int64_t* keep) {
+  for (int q = threadIdx.x; q < p.n_alloc; q += kTopkThreads) {
     if (q < begin) {
       keep[q] = q;
       store_bias(p, b, q, 0.f);
@@ -198,6 +216,120 @@ __global__ void __launch_bounds__(kTopkThreads, 1) topk_select_kernel(const Topk
       store_bias(p, b, q, -1e9f);
     }
   }
+}
+
+// Requests with n_state <= kTopkThreads * KPT: thread t owns the KPT
+// consecutive scores [t*KPT, (t+1)*KPT), loaded once (16-byte loads when
+// aligned) and kept in registers as order-preserving keys through the four
+// digit passes and the index-order compaction.
+template <int KPT>
+__global__ void __launch_bounds__(kTopkThreads, 1) topk_select_reg_kernel(const TopkParams p) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_warp[32];
+  __shared__ uint32_t s_bin, s_need, s_total;
+
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = p.n_state[b];
+  const int K = p.k[b];
+  const int begin = p.begin[b];
+  const int end = begin + n;
+  const int n_kept = begin + K + (p.seq_len[b] - end);
+  const float* sc = p.scores + (int64_t)b * p.s_sb;
+  const int i0 = tid * KPT;
+
+  uint32_t key[KPT];
+  const bool vec = ((reinterpret_cast<uintptr_t>(sc) & 15) == 0) && (i0 + KPT <= n);
+  if (vec) {
+#pragma unroll
+    for (int e = 0; e < KPT; e += 4) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(sc + i0 + e));
+      key[e] = order_key(f.x); key[e + 1] = order_key(f.y);
+      key[e + 2] = order_key(f.z); key[e + 3] = order_key(f.w);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < KPT; ++e) key[e] = order_key((i0 + e < n) ? __ldg(sc + i0 + e) : 0.f);
+  }
+  const int n_mine = max(0, min(KPT, n - i0));  // valid keys of this thread
+
+  uint32_t prefix = 0, mask = 0, need = (uint32_t)K;
+#pragma unroll 1
+  for (int d = 3; d >= 0; --d) {
+    const int shift = 8 * d;
+    if (tid < 256) hist[tid] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < KPT; ++e) {
+      const uint32_t digit = (e < n_mine && (key[e] & mask) == prefix) ? (key[e] >> shift) & 255u : 256u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+      if (digit < 256 && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+    }
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t c[8], sum = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        c[e] = hist[255 - (lane * 8 + e)];
+        sum += c[e];
+      }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      const uint32_t excl = incl - sum;
+      if (excl < need && need <= incl) {
+        uint32_t run = excl;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (run + c[e] >= need) {
+            s_bin = 255 - (lane * 8 + e);
+            s_need = need - run;
+            break;
+          }
+          run += c[e];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= s_bin << shift;
+    mask |= 255u << shift;
+    need = s_need;
+  }
+  const uint32_t T = prefix;
+
+  uint32_t n_gt = 0, n_eq = 0;
+#pragma unroll
+  for (int e = 0; e < KPT; ++e) {
+    n_gt += (e < n_mine && key[e] > T);
+    n_eq += (e < n_mine && key[e] == T);
+  }
+  const uint32_t eq_before = block_excl_scan(n_eq, s_warp, &s_total);
+  const uint32_t take_eq = (need > eq_before) ? min(n_eq, need - eq_before) : 0u;
+  const uint32_t out_before = block_excl_scan(n_gt + take_eq, s_warp, &s_total);
+
+  int64_t* keep = p.keep + (int64_t)b * p.keep_sb;
+  int64_t* tl = p.topk_local ? p.topk_local + (int64_t)b * p.tl_sb : nullptr;
+  uint32_t rank = out_before, eq_seen = 0;
+#pragma unroll
+  for (int e = 0; e < KPT; ++e) {
+    if (e < n_mine) {
+      bool sel = key[e] > T;
+      if (key[e] == T) {
+        sel = eq_seen < take_eq;
+        ++eq_seen;
+      }
+      if (sel) {
+        keep[begin + rank] = begin + i0 + e;
+        if (tl) tl[rank] = i0 + e;
+        store_bias(p, b, begin + (int)rank, key_value(key[e]));
+        ++rank;
+      }
+    }
+  }
+  topk_write_fixed(p, b, begin, K, end, n_kept, keep);
 }
 
 }  // namespace tg
