@@ -84,7 +84,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu_index)],
+                 "-lms", "50", "-i", str(self.gpu_index)],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -288,6 +288,13 @@ def main():
             pg.barrier()
         torch.cuda.synchronize(dev)
 
+    def sum_over_ranks(x: float) -> float:
+        if pg is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.SUM)
+        return float(t.item())
+
     def max_over_ranks(x: float) -> float:
         if pg is None:
             return x
@@ -324,7 +331,7 @@ def main():
     ms_step = ms / args.steps
     value = world * SEQ_LEN * args.steps / (ms / 1e3)
     a_flops, a_ms, a_n = meter.attention_summary()
-    launches = meter.launches
+    launches = int(sum_over_ranks(meter.launches))
 
     # ---- end to end through the public API (host ids in, first token out)
     for _ in range(args.warmup):
@@ -362,7 +369,7 @@ def main():
                      "traffic": None},
         "clocks": clk,
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:   # rank 0 at N=1 only
         tps, sec, threads = cpu_oracle_sample(tm, steps=1, warmup=0)
         line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
                                 "sample": sample_desc(), "seconds": sec}
