@@ -173,6 +173,35 @@ typedef struct {
 int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t* idx,
                    int64_t idx_sb, int B, int n_rows, const int32_t* n_valid, void* stream);
 
+/*
+ * Decoder-layer glue (SURVEY next row: fused prologues). Each replaces an
+ * eager op chain of the transformers Qwen3 layer that the reference runs
+ * around its patched attention (tokengate/e2e_gate/attn/qwen3_flex_attention.py:
+ * 539-551 q/k projections + q_norm/k_norm + apply_rotary_pos_emb, :646-648
+ * o_proj; transformers Qwen3DecoderLayer residual adds, Qwen3RMSNorm,
+ * Qwen3MLP), keeping its bf16 rounding points. bf16 tensors, 16-byte aligned
+ * rows, strides in elements.
+ */
+
+/* h_out = bf16(h_in + delta) (skipped when delta is NULL; h_out may alias
+ * h_in); x_out = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))) with h the
+ * updated row (skipped when x_out is NULL). hidden: 256 * {1,2,4,8,10,16,20}. */
+int tg_add_rmsnorm(const void* h_in, int64_t ld_h_in, const void* delta, int64_t ld_delta,
+                   void* h_out, int64_t ld_h_out, void* x_out, int64_t ld_x, const void* weight,
+                   int64_t rows, int hidden, float eps, void* stream);
+
+/* In place on a fused [q heads | k heads | ...] projection of `rows` tokens
+ * (row stride ld_row): every q and k head (head_dim 128) is RMS-normalised
+ * with its norm weight, then rotated: x = bf16(bf16(y*cos) + bf16(rotate_half(y)*sin)).
+ * cos/sin: (B, seq, 128) bf16 with batch/row strides cs_sb/cs_ss; rows = B*seq. */
+int tg_qk_norm_rope(void* qkv, int64_t rows, int64_t ld_row, int n_q_heads, int n_k_heads, int seq,
+                    const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
+                    int64_t cs_sb, int64_t cs_ss, int head_dim, float eps, void* stream);
+
+/* out[r, :] = bf16(bf16(silu(g)) * u) for a fused row [g (inter) | u (inter)]. */
+int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_t rows, int64_t inter,
+                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,111 @@
+"""Fused decoder-layer glue vs the transformers Qwen3 ops it replaces, on the GPU.
+
+The reference computes these with transformers' modules (Qwen3RMSNorm, the
+decoder-layer residual adds, apply_rotary_pos_emb, Qwen3MLP), so those
+modules, run on the same bf16 inputs, are the checker. Tolerances: the
+residual add is bit-exact; normalised outputs may differ by one bf16 ulp
+where the variance (a 2048- or 128-term fp32 sum) rounds differently in
+torch's reduction order — checked as max relative difference <= 2^-7 and
+>= 99% of elements bit-identical.
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm, apply_rotary_pos_emb
+
+from tokengate_b200 import ops
+from tokengate_b200 import prefill as tgp
+
+pytestmark = pytest.mark.gpu
+
+
+def _close_bf16(got, ref, min_exact=0.99):
+    g, r = got.float(), ref.float()
+    rel = ((g - r).abs() / r.abs().clamp_min(1e-6)).max().item()
+    exact = (got.view(torch.int16) == ref.view(torch.int16)).float().mean().item()
+    assert rel <= 2 ** -7 or (g - r).abs().max().item() < 1e-6, f"max rel {rel}"
+    assert exact >= min_exact, f"only {exact:.4f} bit-identical"
+
+
+@pytest.mark.parametrize("H", [2048, 4096, 512])
+def test_add_rmsnorm(cuda, H):
+    g = torch.Generator(device=cuda).manual_seed(H)
+    h = torch.randn(3, 257, H, device=cuda, generator=g).to(torch.bfloat16)
+    d = torch.randn(3, 257, H, device=cuda, generator=g).to(torch.bfloat16)
+    norm = Qwen3RMSNorm(H, eps=1e-6).to(cuda).to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.1 * torch.randn(H, device=cuda, generator=g))
+        ref_h = h + d
+        ref_x = norm(ref_h)
+    h2 = h.clone()
+    out_h, x = ops.add_rmsnorm(h2, d, norm.weight, 1e-6, h_out=h2)
+    assert out_h.data_ptr() == h2.data_ptr()
+    assert torch.equal(out_h, ref_h)
+    _close_bf16(x, ref_x)
+    # norm only, and add only
+    _, x0 = ops.add_rmsnorm(h, None, norm.weight, 1e-6)
+    _close_bf16(x0, norm(h))
+    h3, none = ops.add_rmsnorm(h.clone(), d, None, 0.0, want_x=False)
+    assert none is None and torch.equal(h3, ref_h)
+
+
+def test_qk_norm_rope(cuda):
+    from transformers.models.qwen3.configuration_qwen3 import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+    B, S, nq, nkv, D = 2, 300, 16, 8, 128
+    g = torch.Generator(device=cuda).manual_seed(1)
+    qkv = torch.randn(B, S, nq + 2 * nkv, D, device=cuda, generator=g).to(torch.bfloat16)
+    qn = Qwen3RMSNorm(D, eps=1e-6).to(cuda).to(torch.bfloat16)
+    kn = Qwen3RMSNorm(D, eps=1e-6).to(cuda).to(torch.bfloat16)
+    with torch.no_grad():
+        qn.weight.copy_(1 + 0.2 * torch.randn(D, device=cuda, generator=g))
+        kn.weight.copy_(1 + 0.2 * torch.randn(D, device=cuda, generator=g))
+    cfg = Qwen3Config(hidden_size=2048, num_attention_heads=nq, num_key_value_heads=nkv, head_dim=D,
+                      rope_theta=1e6)
+    rope = Qwen3RotaryEmbedding(cfg).to(cuda)
+    pos = torch.stack([torch.arange(S), torch.sort(torch.randperm(32768)[:S]).values]).to(cuda)
+    cos, sin = rope(qkv, pos)
+    with torch.no_grad():
+        q_ref, k_ref = apply_rotary_pos_emb(qn(qkv[:, :, :nq]).transpose(1, 2),
+                                            kn(qkv[:, :, nq:nq + nkv]).transpose(1, 2), cos, sin)
+    got = qkv.clone()
+    ops.qk_norm_rope(got, nq, nkv, qn.weight, kn.weight, cos, sin, 1e-6)
+    _close_bf16(got[:, :, :nq], q_ref.transpose(1, 2))
+    _close_bf16(got[:, :, nq:nq + nkv], k_ref.transpose(1, 2))
+    assert torch.equal(got[:, :, nq + nkv:], qkv[:, :, nq + nkv:])   # v untouched
+
+
+def test_silu_mul(cuda):
+    g = torch.Generator(device=cuda).manual_seed(2)
+    gu = (torch.randn(5, 77, 2 * 6144, device=cuda, generator=g) * 3).to(torch.bfloat16)
+    out = ops.silu_mul(gu)
+    ref = F.silu(gu[..., :6144]) * gu[..., 6144:]
+    _close_bf16(out, ref, min_exact=0.98)
+
+
+def test_fused_prefill_matches_module_path(cuda):
+    from tokengate_b200.inference import load_model
+    small = dict(hidden_size=1024, intermediate_size=2048, num_hidden_layers=4, num_attention_heads=8,
+                 num_key_value_heads=4, head_dim=128, vocab_size=2000, rope_theta=1e6)
+    tm = load_model(base_model=small, gate_layer=1, device=cuda, seed=5)
+    g = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(0, 2000, (n,), generator=g).tolist() for n in (900, 611)]
+    starts, ends = [30, 11], [870, 600]
+    logits = {}
+    for fused in (False, True):
+        seen = []
+        hk = tm.model.lm_head.register_forward_hook(lambda m, a, o: seen.append(o.detach().float()))
+        try:
+            out = tgp.prefill_batch_for_decode(tm.model, tm.gate, prompts, starts, ends, 1, 64, fused=fused)
+        finally:
+            hk.remove()
+        logits[fused] = (out, seen[-1])
+    (f0, _, k0, n0, _), l0 = logits[False]
+    (f1, _, k1, n1, _), l1 = logits[True]
+    assert n0 == n1
+    for b in range(2):
+        overlap = len(set(k0[b, :n0[b]].tolist()) & set(k1[b, :n1[b]].tolist())) / n0[b]
+        assert overlap >= 0.95
+    cos = (l0 * l1).sum() / (l0.norm() * l1.norm())
+    assert cos.item() >= 0.999, cos.item()
+    assert (l0 - l1).abs().max().item() <= 0.15

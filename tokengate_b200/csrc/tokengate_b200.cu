@@ -16,6 +16,7 @@
 #include "gate_score.cuh"
 #include "topk_select.cuh"
 #include "gather_rows.cuh"
+#include "layer_glue.cuh"
 
 // Bit flags set by kernels whose bounded waits gave up (see ptx.cuh).
 __device__ unsigned int g_tg_device_error = 0;
@@ -40,6 +41,17 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 unsigned int* g_err_ptr[kMaxDevices] = {};
 bool g_attn_attr_set[kMaxDevices] = {};
+
+int sm_count() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+int64_t resident_blocks(int64_t needed, int per_sm) {
+  const int64_t cap = (int64_t)sm_count() * per_sm;
+  return needed < cap ? (needed < 1 ? 1 : needed) : cap;
+}
 
 int current_device(int* dev) {
   cudaError_t e = cudaGetDevice(dev);
@@ -398,6 +410,111 @@ int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gather launch");
   }
+  return TG_OK;
+}
+
+int tg_add_rmsnorm(const void* h_in, int64_t ld_h_in, const void* delta, int64_t ld_delta,
+                   void* h_out, int64_t ld_h_out, void* x_out, int64_t ld_x, const void* weight,
+                   int64_t rows, int hidden, float eps, void* stream) {
+  if (h_in == nullptr || (delta != nullptr && h_out == nullptr) || (x_out != nullptr && weight == nullptr))
+    return fail(TG_ERR_INVALID_ARGUMENT, "add_rmsnorm: NULL argument");
+  if (delta == nullptr && x_out == nullptr) return fail(TG_ERR_INVALID_ARGUMENT, "add_rmsnorm: nothing to do");
+  if (rows < 0) return fail(TG_ERR_INVALID_ARGUMENT, "add_rmsnorm: rows=%lld", (long long)rows);
+  const int nv = hidden / 256;
+  if (hidden % 256 != 0 || !(nv == 1 || nv == 2 || nv == 4 || nv == 8 || nv == 10 || nv == 16 || nv == 20))
+    return fail(TG_ERR_UNSUPPORTED, "add_rmsnorm: hidden %d not served", hidden);
+  const uintptr_t m = reinterpret_cast<uintptr_t>(h_in) | reinterpret_cast<uintptr_t>(delta) |
+                      reinterpret_cast<uintptr_t>(h_out) | reinterpret_cast<uintptr_t>(x_out) |
+                      reinterpret_cast<uintptr_t>(weight);
+  if ((m & 15) || ((ld_h_in | ld_delta | ld_h_out | ld_x) & 7))
+    return fail(TG_ERR_ALIGNMENT, "add_rmsnorm: pointers 16-byte aligned, strides multiples of 8 needed");
+  if (rows == 0) return TG_OK;
+  tg::RmsParams p;
+  p.h_in = static_cast<const __nv_bfloat16*>(h_in);
+  p.delta = static_cast<const __nv_bfloat16*>(delta);
+  p.h_out = static_cast<__nv_bfloat16*>(h_out);
+  p.x_out = static_cast<__nv_bfloat16*>(x_out);
+  p.w = static_cast<const __nv_bfloat16*>(weight);
+  p.rows = rows;
+  p.ld_h_in = ld_h_in;
+  p.ld_delta = ld_delta;
+  p.ld_h_out = ld_h_out;
+  p.ld_x = ld_x;
+  p.eps = eps;
+  p.inv_hidden = 1.f / (float)hidden;
+  const int64_t blocks = resident_blocks((rows + 7) / 8, 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (nv) {
+    case 1: tg::add_rmsnorm_kernel<1><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+    case 2: tg::add_rmsnorm_kernel<2><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+    case 4: tg::add_rmsnorm_kernel<4><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+    case 8: tg::add_rmsnorm_kernel<8><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+    case 10: tg::add_rmsnorm_kernel<10><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+    case 16: tg::add_rmsnorm_kernel<16><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+    default: tg::add_rmsnorm_kernel<20><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "add_rmsnorm launch");
+  return TG_OK;
+}
+
+int tg_qk_norm_rope(void* qkv, int64_t rows, int64_t ld_row, int n_q_heads, int n_k_heads, int seq,
+                    const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
+                    int64_t cs_sb, int64_t cs_ss, int head_dim, float eps, void* stream) {
+  if (qkv == nullptr || q_norm_w == nullptr || k_norm_w == nullptr || cos == nullptr || sin == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope: NULL argument");
+  if (head_dim != 128) return fail(TG_ERR_UNSUPPORTED, "qk_norm_rope: head_dim %d (only 128)", head_dim);
+  if (rows < 0 || n_q_heads < 0 || n_k_heads < 0 || seq < 1 || (rows % seq) != 0)
+    return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope: rows %lld must be a multiple of seq %d",
+                (long long)rows, seq);
+  if (ld_row < (int64_t)(n_q_heads + n_k_heads) * 128)
+    return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope: row stride shorter than the q and k heads");
+  const uintptr_t m = reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(q_norm_w) |
+                      reinterpret_cast<uintptr_t>(k_norm_w) | reinterpret_cast<uintptr_t>(cos) |
+                      reinterpret_cast<uintptr_t>(sin);
+  if ((m & 15) || ((ld_row | cs_sb | cs_ss) & 7))
+    return fail(TG_ERR_ALIGNMENT, "qk_norm_rope: pointers 16-byte aligned, strides multiples of 8 needed");
+  if (rows == 0 || n_q_heads + n_k_heads == 0) return TG_OK;
+  tg::QkRopeParams p;
+  p.qkv = static_cast<__nv_bfloat16*>(qkv);
+  p.rows = rows;
+  p.ld_row = ld_row;
+  p.n_q = n_q_heads;
+  p.n_k = n_k_heads;
+  p.seq = seq;
+  p.q_w = static_cast<const __nv_bfloat16*>(q_norm_w);
+  p.k_w = static_cast<const __nv_bfloat16*>(k_norm_w);
+  p.cos = static_cast<const __nv_bfloat16*>(cos);
+  p.sin = static_cast<const __nv_bfloat16*>(sin);
+  p.cs_sb = cs_sb;
+  p.cs_ss = cs_ss;
+  p.eps = eps;
+  const int64_t blocks = resident_blocks((rows * (n_q_heads + n_k_heads) + 7) / 8, 8);
+  tg::qk_norm_rope_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "qk_norm_rope launch");
+  return TG_OK;
+}
+
+int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_t rows, int64_t inter,
+                void* stream) {
+  if (gu == nullptr || out == nullptr) return fail(TG_ERR_INVALID_ARGUMENT, "silu_mul: NULL argument");
+  if (rows < 0 || inter < 8 || (inter & 7)) return fail(TG_ERR_INVALID_ARGUMENT, "silu_mul: inter %lld must be a positive multiple of 8", (long long)inter);
+  if (ld_gu < 2 * inter || ld_out < inter) return fail(TG_ERR_INVALID_ARGUMENT, "silu_mul: strides too short");
+  if (((reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(out)) & 15) || ((ld_gu | ld_out) & 7))
+    return fail(TG_ERR_ALIGNMENT, "silu_mul: pointers 16-byte aligned, strides multiples of 8 needed");
+  if (rows == 0) return TG_OK;
+  tg::SiluParams p;
+  p.gu = static_cast<const __nv_bfloat16*>(gu);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.rows = rows;
+  p.inter = inter;
+  p.ld_gu = ld_gu;
+  p.ld_out = ld_out;
+  const int64_t blocks = resident_blocks((rows * (inter / 8) + 255) / 256, 8);
+  tg::silu_mul_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
   return TG_OK;
 }
 

@@ -1,0 +1,108 @@
+"""Fused Qwen3 decoder layer for the gated prefill (SURVEY next row: fused prologues).
+
+The transformers Qwen3DecoderLayer the reference runs (with its attention
+patched, tokengate/e2e_gate/attn/qwen3_flex_attention.py:475-652) issues ~30
+elementwise kernels per layer around 7 GEMMs. Here one layer is
+
+    h, x  = add_rmsnorm(h, delta_prev, input_layernorm)     # residual add + RMSNorm
+    qkv   = x @ [Wq; Wk; Wv]^T                              # one GEMM
+    qk_norm_rope(qkv)                                       # q/k RMSNorm + RoPE, in place
+    a     = keybias_attention(q, k, v, gate bias)           # tcgen05 kernel
+    h, x2 = add_rmsnorm(h, a @ Wo^T, post_attention_layernorm)
+    act   = silu_mul(x2 @ [Wgate; Wup]^T)                   # one GEMM + one glue kernel
+    delta = act @ Wdown^T                                   # added by the next layer
+
+with the module's own weights: the q/k/v and gate/up weights are
+concatenated once and the modules' parameters re-pointed to views of the
+concatenation, so nothing is duplicated and the model stays usable through
+transformers. Q/K/V stay views of the fused projection; the prefill cache
+keeps K and V as such views.
+"""
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+
+class FusedLayerWeights:
+    """Views of one Qwen3DecoderLayer's parameters in the fused layout."""
+
+    def __init__(self, layer):
+        a, m = layer.self_attn, layer.mlp
+        for lin in (a.q_proj, a.k_proj, a.v_proj, a.o_proj, m.gate_proj, m.up_proj, m.down_proj):
+            if lin.bias is not None:
+                raise NotImplementedError("projection biases are not served by the fused layer")
+        cfg = a.config
+        self.head_dim = a.head_dim
+        if self.head_dim != 128:
+            raise NotImplementedError(f"head_dim {self.head_dim}: the B200 kernels serve 128")
+        self.n_q = cfg.num_attention_heads
+        self.n_kv = cfg.num_key_value_heads
+        self.eps = float(layer.input_layernorm.variance_epsilon)
+        self.qk_eps = float(a.q_norm.variance_epsilon)
+        self.wqkv = self._fuse(a.q_proj, a.k_proj, a.v_proj)
+        self.wgu = self._fuse(m.gate_proj, m.up_proj)
+        self.wo = a.o_proj.weight
+        self.wdown = m.down_proj.weight
+        self.in_w = layer.input_layernorm.weight
+        self.post_w = layer.post_attention_layernorm.weight
+        self.q_norm_w = a.q_norm.weight
+        self.k_norm_w = a.k_norm.weight
+        self.inter = m.gate_proj.weight.shape[0]
+
+    @staticmethod
+    def _fuse(*lins):
+        ws = [l.weight for l in lins]
+        base = ws[0]
+        # already fused (an earlier call re-pointed them as consecutive views of
+        # one buffer): reuse that buffer
+        offs, expect = [], base.storage_offset()
+        for w in ws:
+            offs.append(w.storage_offset() == expect and w.is_contiguous()
+                        and w.untyped_storage().data_ptr() == base.untyped_storage().data_ptr())
+            expect += w.numel()
+        if all(offs):
+            total = sum(w.shape[0] for w in ws)
+            return base.new_empty(0).set_(base.untyped_storage(), base.storage_offset(),
+                                          (total, base.shape[1]))
+        fused = torch.cat([w.detach() for w in ws], dim=0).contiguous()
+        off = 0
+        for l, w in zip(lins, ws):
+            n = w.shape[0]
+            l.weight.data = fused[off:off + n]
+            off += n
+        return fused
+
+
+def fused_weights(model):
+    """Per-layer fused weight views, built once and cached on the model."""
+    fw = getattr(model, "_tg_fused", None)
+    if fw is None:
+        fw = [FusedLayerWeights(layer) for layer in model.model.layers]
+        model._tg_fused = fw
+    return fw
+
+
+def layer_forward(lw: FusedLayerWeights, h: torch.Tensor, delta: Optional[torch.Tensor],
+                  cos: torch.Tensor, sin: torch.Tensor, cache, layer_idx: int,
+                  gate_bias: Optional[torch.Tensor] = None,
+                  q_row_scale: Optional[torch.Tensor] = None):
+    """One decoder layer. h: (B, S, H) residual stream (updated in place when
+    delta is given); delta: the previous layer's MLP output or None. Returns
+    (h, delta') with delta' this layer's MLP output, not yet added."""
+    B, S, H = h.shape
+    h, x = ops.add_rmsnorm(h, delta, lw.in_w, lw.eps, h_out=h if delta is not None else None)
+    qkv = F.linear(x, lw.wqkv).view(B, S, lw.n_q + 2 * lw.n_kv, lw.head_dim)
+    ops.qk_norm_rope(qkv, lw.n_q, lw.n_kv, lw.q_norm_w, lw.k_norm_w, cos, sin, lw.qk_eps)
+    q = qkv[:, :, :lw.n_q]
+    k = qkv[:, :, lw.n_q:lw.n_q + lw.n_kv]
+    v = qkv[:, :, lw.n_q + lw.n_kv:]
+    if cache is not None:
+        k, v = cache.update_tok(k, v, layer_idx)
+    a = ops.keybias_attention(q, k, v, bias=gate_bias, causal=True, q_row_scale=q_row_scale)
+    o = F.linear(a.view(B, S, -1), lw.wo)
+    h, x2 = ops.add_rmsnorm(h, o, lw.post_w, lw.eps, h_out=h)
+    act = ops.silu_mul(F.linear(x2, lw.wgu))
+    return h, F.linear(act, lw.wdown)

@@ -285,6 +285,95 @@ def gather_rows(specs: Sequence[_lib.GatherTensor], idx: torch.Tensor, n_valid: 
                                     _i32_array(n_valid), _stream(idx)))
 
 
+# ----------------------------------------------------------------- layer glue
+def _rows2d(name, t):
+    if t.dim() < 2 or t.stride(-1) != 1:
+        raise ValueError(f"{name} must have a contiguous last dim")
+    lead = t.shape[:-1]
+    # every leading dim must collapse onto one row stride
+    flat = t.reshape(-1, t.shape[-1]) if t.is_contiguous() else None
+    if flat is None:
+        if t.dim() != 2:
+            raise ValueError(f"{name}: non-contiguous inputs must be 2-D (rows, hidden)")
+        flat = t
+    return flat, lead
+
+
+def add_rmsnorm(h: torch.Tensor, delta: Optional[torch.Tensor], weight: Optional[torch.Tensor],
+                eps: float, h_out: Optional[torch.Tensor] = None, want_x: bool = True):
+    """h_out = bf16(h + delta) (if delta); x = bf16(w * bf16(h_out * rsqrt(mean(h_out^2) + eps))).
+
+    Returns (h_out, x); h_out is h itself when delta is None. h_out may be h (in place).
+    """
+    _require_cuda("h", h, torch.bfloat16)
+    hf, lead = _rows2d("h", h)
+    H = hf.shape[1]
+    d_ptr, d_ld = None, 0
+    if delta is not None:
+        _require_cuda("delta", delta, torch.bfloat16)
+        if delta.shape != h.shape:
+            raise ValueError("delta must match h")
+        df, _ = _rows2d("delta", delta)
+        d_ptr, d_ld = df.data_ptr(), df.stride(0)
+        if h_out is None:
+            h_out = torch.empty_like(h)
+        hof, _ = _rows2d("h_out", h_out)
+    else:
+        h_out, hof = h, hf
+    x = None
+    x_ptr, x_ld, w_ptr = None, 0, None
+    if want_x:
+        _require_cuda("weight", weight, torch.bfloat16)
+        x = torch.empty(h.shape, dtype=torch.bfloat16, device=h.device)
+        x_ptr, x_ld, w_ptr = x.data_ptr(), H, weight.data_ptr()
+    L = _lib.lib()
+    with _device_ctx(h):
+        _lib.check(L.tg_add_rmsnorm(hf.data_ptr(), hf.stride(0), d_ptr, d_ld,
+                                    hof.data_ptr() if delta is not None else None,
+                                    hof.stride(0) if delta is not None else 0,
+                                    x_ptr, x_ld, w_ptr, hf.shape[0], H, float(eps), _stream(h)))
+    return h_out, x
+
+
+def qk_norm_rope(qkv: torch.Tensor, n_q: int, n_k: int, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
+                 cos: torch.Tensor, sin: torch.Tensor, eps: float) -> None:
+    """In place on qkv (B, S, heads, 128): RMS-norm + RoPE of the first n_q (q) and next n_k (k) heads.
+
+    cos/sin: (B, S, 128) bf16 (the rotary embedding of the rows' positions).
+    """
+    _require_cuda("qkv", qkv, torch.bfloat16)
+    if qkv.dim() != 4 or qkv.shape[-1] != 128 or qkv.stride(-1) != 1 or qkv.stride(-2) != 128:
+        raise ValueError("qkv must be (B, S, heads, 128) with contiguous heads")
+    B, S = qkv.shape[0], qkv.shape[1]
+    if qkv.stride(0) != S * qkv.stride(1):
+        raise ValueError("qkv rows must be evenly strided across the batch")
+    for nm, t in (("cos", cos), ("sin", sin)):
+        _require_cuda(nm, t, torch.bfloat16)
+        if t.shape != (B, S, 128) or t.stride(-1) != 1:
+            raise ValueError(f"{nm} must be (B, S, 128) with a contiguous last dim")
+    if cos.stride() != sin.stride():
+        raise ValueError("cos and sin must share strides")
+    L = _lib.lib()
+    with _device_ctx(qkv):
+        _lib.check(L.tg_qk_norm_rope(qkv.data_ptr(), B * S, qkv.stride(1), int(n_q), int(n_k), S,
+                                     q_norm_w.data_ptr(), k_norm_w.data_ptr(), cos.data_ptr(),
+                                     sin.data_ptr(), cos.stride(0), cos.stride(1), 128, float(eps),
+                                     _stream(qkv)))
+
+
+def silu_mul(gu: torch.Tensor) -> torch.Tensor:
+    """gu (..., 2*I) = [gate | up] -> bf16(bf16(silu(gate)) * up) (..., I)."""
+    _require_cuda("gu", gu, torch.bfloat16)
+    gf, lead = _rows2d("gu", gu)
+    inter = gf.shape[1] // 2
+    out = torch.empty(*lead, inter, dtype=torch.bfloat16, device=gu.device)
+    L = _lib.lib()
+    with _device_ctx(gu):
+        _lib.check(L.tg_silu_mul(gf.data_ptr(), gf.stride(0), out.data_ptr(), inter, gf.shape[0], inter,
+                                 _stream(gu)))
+    return out
+
+
 def device_error(clear: bool = False) -> int:
     """Flags recorded by kernels whose bounded waits gave up on the current device (synchronises)."""
     return _lib.device_error(torch.cuda.current_stream().cuda_stream, clear)

@@ -28,6 +28,7 @@ import torch
 
 from . import ops
 from .gate import readout_vector
+from .layers import fused_weights, layer_forward
 from .model import PrefillCache, set_attn_scale_for_layers, set_gate_bias_for_layers
 
 # Phase-2 length bucket (the reference's set_phase2_bucket, gate_forward.py:531-546):
@@ -55,7 +56,11 @@ def _ids_to_device(prompt_ids_list, device) -> torch.Tensor:
 def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequence,
                              article_starts: Sequence[int], article_ends: Sequence[int],
                              gate_layer: int, K: Union[int, Sequence[int]],
-                             prune_below_gate: bool = False):
+                             prune_below_gate: bool = False, fused: Optional[bool] = None):
+    """fused: run the decoder layers through the fused glue kernels
+    (tokengate_b200.layers); None picks it whenever the gate has no learned
+    attention scale. False runs the transformers layers with the patched
+    attention module (the reference's structure)."""
     B = len(prompt_ids_list)
     if B < 1:
         raise ValueError("empty batch")
@@ -73,6 +78,12 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
         if not 0 <= starts[b] < ends[b] <= lens[b]:
             raise ValueError(f"request {b}: state span [{starts[b]}, {ends[b]}) invalid for length {lens[b]}")
     max_seq_len = max(lens)
+    has_attn_scale = hasattr(gate, "attn_scale_eff") and not getattr(gate, "_baseline_no_bias_scale", False)
+    if fused is None:
+        fused = not has_attn_scale
+    if fused and has_attn_scale:
+        raise NotImplementedError("the fused layer path serves gates without a learned attention scale")
+    fw = fused_weights(model) if fused else None
 
     # ---- Phase 1
     ids = _ids_to_device(prompt_ids_list, device)
@@ -81,9 +92,17 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
     position_ids = torch.arange(max_seq_len, device=device).unsqueeze(0).expand(B, -1)
     pe = inner.rotary_emb(hidden, position_ids)
     cache = PrefillCache(n_layers)
-    for i in range(gate_layer + 1):
-        hidden = inner.layers[i](hidden, attention_mask=None, position_ids=position_ids,
-                                 past_key_values=cache, use_cache=True, position_embeddings=pe)
+    if fused:
+        cos, sin = pe
+        delta = None
+        for i in range(gate_layer + 1):
+            hidden, delta = layer_forward(fw[i], hidden, delta, cos, sin, cache, i)
+        hidden, _ = ops.add_rmsnorm(hidden, delta, None, 0.0, h_out=hidden, want_x=False)
+        del delta, cos, sin
+    else:
+        for i in range(gate_layer + 1):
+            hidden = inner.layers[i](hidden, attention_mask=None, position_ids=position_ids,
+                                     past_key_values=cache, use_cache=True, position_embeddings=pe)
     del pe
 
     # ---- score + select
@@ -126,19 +145,30 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
     # The reference hands the bf16 bias to every layer and each converts it to
     # fp32 (_bias_bhs); converting once here gives the same values.
     gate_bias = bias_row.float()
-    set_gate_bias_for_layers(model, gate_layer + 1, n_layers, gate_bias, per_head=False)
-    attn_scale = None
-    if hasattr(gate, "attn_scale_eff") and not getattr(gate, "_baseline_no_bias_scale", False):
-        attn_scale = gate.attn_scale_eff()
-    set_attn_scale_for_layers(model, gate_layer + 1, n_layers, attn_scale)
     pe2 = inner.rotary_emb(hs_pruned, kept_positions)
-    for i in range(gate_layer + 1, n_layers):
-        hs_pruned = inner.layers[i](hs_pruned, attention_mask=None, position_ids=kept_positions,
-                                    past_key_values=cache, use_cache=True, position_embeddings=pe2)
+    last_valid = torch.tensor([n - 1 for n in n_kepts], device=device)
+    rows = torch.arange(B, device=device)
+    if fused:
+        bias3 = gate_bias.unsqueeze(1)                      # (B, 1, n_alloc): one row for all heads
+        cos2, sin2 = pe2
+        delta = None
+        for i in range(gate_layer + 1, n_layers):
+            hs_pruned, delta = layer_forward(fw[i], hs_pruned, delta, cos2, sin2, cache, i,
+                                             gate_bias=bias3)
+        # final residual add + norm only on the rows the head reads
+        h_last = hs_pruned[rows, last_valid]
+        _, hs_last = ops.add_rmsnorm(h_last, delta[rows, last_valid], inner.norm.weight,
+                                     float(inner.norm.variance_epsilon))
+    else:
+        set_gate_bias_for_layers(model, gate_layer + 1, n_layers, gate_bias, per_head=False)
+        attn_scale = gate.attn_scale_eff() if has_attn_scale else None
+        set_attn_scale_for_layers(model, gate_layer + 1, n_layers, attn_scale)
+        for i in range(gate_layer + 1, n_layers):
+            hs_pruned = inner.layers[i](hs_pruned, attention_mask=None, position_ids=kept_positions,
+                                        past_key_values=cache, use_cache=True, position_embeddings=pe2)
+        hs_last = inner.norm(hs_pruned[rows, last_valid])
 
     # ---- head
-    last_valid = torch.tensor([n - 1 for n in n_kepts], device=device)
-    hs_last = inner.norm(hs_pruned[torch.arange(B, device=device), last_valid])
     first_tokens = model.lm_head(hs_last).argmax(-1, keepdim=True)
     if n_alloc != max_n_kept:
         for i in range(gate_layer + 1, n_layers):
