@@ -122,7 +122,8 @@ class KernelMeter:
         from tokengate_b200 import ops
         self.ops = ops
         self.orig = {n: getattr(ops, n) for n in ("keybias_attention", "gate_score", "topk_select",
-                                                  "gather_rows")}
+                                                  "gather_rows", "add_rmsnorm", "qk_norm_rope",
+                                                  "silu_mul")}
         self.active = False
         self.launches = 0
         self.attn = []   # (flops, start_event, end_event)
@@ -160,6 +161,9 @@ class KernelMeter:
         ops.gate_score = counted("gate_score", lambda a, kw: (len(a[2]) + 127) // 128)
         ops.topk_select = counted("topk_select", lambda a, kw: (a[0].shape[0] + 63) // 64)
         ops.gather_rows = counted("gather_rows", lambda a, kw: (a[1].shape[0] + 63) // 64)
+        ops.add_rmsnorm = counted("add_rmsnorm", lambda a, kw: 1)
+        ops.qk_norm_rope = counted("qk_norm_rope", lambda a, kw: 1)
+        ops.silu_mul = counted("silu_mul", lambda a, kw: 1)
 
     def attention_summary(self):
         flops = sum(f for f, _, _ in self.attn)

@@ -32,14 +32,17 @@ _NO_PRUNING = 10_000_000
 
 def split_state_span(ids: List[int]):
     """Strip the state sentinels: ids -> (clean_ids, start, end) (gate_forward.py:669-689)."""
-    starts = [i for i, t in enumerate(ids) if t == STATE_START_ID]
-    ends = [i for i, t in enumerate(ids) if t == STATE_END_ID]
-    if len(starts) != 1 or len(ends) != 1 or starts[0] >= ends[0]:
+    ids = list(ids)
+    n_s, n_e = ids.count(STATE_START_ID), ids.count(STATE_END_ID)   # C-speed scans of long prompts
+    s = ids.index(STATE_START_ID) if n_s == 1 else -1
+    e = ids.index(STATE_END_ID) if n_e == 1 else -1
+    if n_s != 1 or n_e != 1 or s >= e:
+        starts = [i for i, t in enumerate(ids) if t == STATE_START_ID]
+        ends = [i for i, t in enumerate(ids) if t == STATE_END_ID]
         raise ValueError(
             "ids carry no valid state span: expected exactly one STATE_START_ID followed by one "
             f"STATE_END_ID (produce ids with apply_chat_template(state=...)); found starts={starts} "
             f"ends={ends}")
-    s, e = starts[0], ends[0]
     clean = list(ids[:s]) + list(ids[s + 1:e]) + list(ids[e + 1:])
     return clean, s, e - 1
 

@@ -22,6 +22,7 @@ The reference's per-request Python loop for scoring/selection/gather and its
 host-side index construction are replaced by three batched launches; no host
 synchronisation happens between Phase 1 and the head.
 """
+import array
 from typing import List, Optional, Sequence, Union
 
 import torch
@@ -48,7 +49,10 @@ def _ids_to_device(prompt_ids_list, device) -> torch.Tensor:
     lens = [len(x) for x in prompt_ids_list]
     host = torch.zeros(B, max(lens), dtype=torch.long, pin_memory=torch.cuda.is_available())
     for b, ids in enumerate(prompt_ids_list):
-        host[b, :lens[b]] = ids if torch.is_tensor(ids) else torch.as_tensor(ids, dtype=torch.long)
+        if torch.is_tensor(ids):
+            host[b, :lens[b]] = ids
+        else:   # list of ints -> int64 buffer without per-element tensor conversion
+            host[b, :lens[b]] = torch.frombuffer(array.array("q", ids), dtype=torch.long)
     return host.to(device, non_blocking=True)
 
 
