@@ -190,13 +190,15 @@ int tg_add_rmsnorm(const void* h_in, int64_t ld_h_in, const void* delta, int64_t
                    void* h_out, int64_t ld_h_out, void* x_out, int64_t ld_x, const void* weight,
                    int64_t rows, int hidden, float eps, void* stream);
 
-/* In place on a fused [q heads | k heads | ...] projection of `rows` tokens
- * (row stride ld_row): every q and k head (head_dim 128) is RMS-normalised
- * with its norm weight, then rotated: x = bf16(bf16(y*cos) + bf16(rotate_half(y)*sin)).
+/* In place on the q projection (rows x n_q_heads x 128, row stride ld_q) and
+ * the k projection (rows x n_k_heads x 128, row stride ld_k) of `rows`
+ * tokens: every head (head_dim 128) is RMS-normalised with its norm weight,
+ * then rotated: x = bf16(bf16(y*cos) + bf16(rotate_half(y)*sin)).
  * cos/sin: (B, seq, 128) bf16 with batch/row strides cs_sb/cs_ss; rows = B*seq. */
-int tg_qk_norm_rope(void* qkv, int64_t rows, int64_t ld_row, int n_q_heads, int n_k_heads, int seq,
-                    const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
-                    int64_t cs_sb, int64_t cs_ss, int head_dim, float eps, void* stream);
+int tg_qk_norm_rope(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k, int n_k_heads,
+                    int64_t rows, int seq, const void* q_norm_w, const void* k_norm_w,
+                    const void* cos, const void* sin, int64_t cs_sb, int64_t cs_ss, int head_dim,
+                    float eps, void* stream);
 
 /* out[r, :] = bf16(bf16(silu(g)) * u) for a fused row [g (inter) | u (inter)]. */
 int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_t rows, int64_t inter,

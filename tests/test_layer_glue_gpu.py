@@ -69,10 +69,14 @@ def test_qk_norm_rope(cuda):
         q_ref, k_ref = apply_rotary_pos_emb(qn(qkv[:, :, :nq]).transpose(1, 2),
                                             kn(qkv[:, :, nq:nq + nkv]).transpose(1, 2), cos, sin)
     got = qkv.clone()
-    ops.qk_norm_rope(got, nq, nkv, qn.weight, kn.weight, cos, sin, 1e-6)
+    ops.qk_norm_rope(got[:, :, :nq], got[:, :, nq:nq + nkv], qn.weight, kn.weight, cos, sin, 1e-6)
     _close_bf16(got[:, :, :nq], q_ref.transpose(1, 2))
     _close_bf16(got[:, :, nq:nq + nkv], k_ref.transpose(1, 2))
     assert torch.equal(got[:, :, nq + nkv:], qkv[:, :, nq + nkv:])   # v untouched
+    # separate q and k buffers
+    q2, k2 = qkv[:, :, :nq].contiguous(), qkv[:, :, nq:nq + nkv].contiguous()
+    ops.qk_norm_rope(q2, k2, qn.weight, kn.weight, cos, sin, 1e-6)
+    assert torch.equal(q2, got[:, :, :nq]) and torch.equal(k2, got[:, :, nq:nq + nkv])
 
 
 def test_silu_mul(cuda):

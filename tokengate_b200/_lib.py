@@ -80,7 +80,8 @@ _SIGNATURES = {
     "tg_topk_select": [_P, _I64, _I32, _P, _P, _P, _P, _I32, _P, _I64, _P, _I64, _I32, _P, _I64, _P],
     "tg_gather_rows": [ctypes.POINTER(GatherTensor), _I32, _P, _I64, _I32, _I32, _P, _P],
     "tg_add_rmsnorm": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I32, _F, _P],
-    "tg_qk_norm_rope": [_P, _I64, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _I64, _I32, _F, _P],
+    "tg_qk_norm_rope": [_P, _I64, _I32, _P, _I64, _I32, _I64, _I32, _P, _P, _P, _P, _I64, _I64, _I32,
+                        _F, _P],
     "tg_silu_mul": [_P, _I64, _P, _I64, _I64, _I64, _P],
 }
 EXPORTED = tuple(_SIGNATURES)

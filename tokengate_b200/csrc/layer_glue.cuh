@@ -7,7 +7,7 @@
 // (tokengate/e2e_gate/attn/qwen3_flex_attention.py:539-551, :646-648):
 //
 //   add_rmsnorm   h <- bf16(h + delta);  x <- bf16(w * bf16(h * rsqrt(mean(h^2) + eps)))
-//   qk_norm_rope  per q/k head of a fused [q | k | v] projection row:
+//   qk_norm_rope  per q head and k head of the projections:
 //                 y <- bf16(w * bf16(x * rsqrt(mean(x^2) + eps)))
 //                 x <- bf16(bf16(y * cos) + bf16(rotate_half(y) * sin))      (in place)
 //   silu_mul      out <- bf16(bf16(silu(g)) * u) for a fused [g | u] row
@@ -104,10 +104,11 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const RmsParams p) {
 }
 
 struct QkRopeParams {
-  __nv_bfloat16* qkv;          // (rows, n_heads_total, 128)
+  __nv_bfloat16* q;            // (rows, n_q, 128), row stride ld_q
+  __nv_bfloat16* k;            // (rows, n_k, 128), row stride ld_k
   int64_t rows;
-  int64_t ld_row;              // row stride (elements)
-  int n_q, n_k;                // q heads then k heads are normalised + rotated
+  int64_t ld_q, ld_k;          // row strides (elements)
+  int n_q, n_k;                // q heads and k heads to normalise + rotate
   int seq;                     // rows per batch entry (cos/sin are (B, seq, 128))
   const __nv_bfloat16* q_w;
   const __nv_bfloat16* k_w;
@@ -128,8 +129,11 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkRopeParams p)
   for (int64_t wi = warp_global; wi < total; wi += n_warps) {
     const int64_t row = wi / heads;
     const int hd = (int)(wi - row * heads);
-    const __nv_bfloat16* w = hd < p.n_q ? p.q_w : p.k_w;
-    uint2* xp = reinterpret_cast<uint2*>(p.qkv + row * p.ld_row + (int64_t)hd * 128) + lane;
+    const bool is_q = hd < p.n_q;
+    const __nv_bfloat16* w = is_q ? p.q_w : p.k_w;
+    __nv_bfloat16* base = is_q ? p.q + row * p.ld_q + (int64_t)hd * 128
+                               : p.k + row * p.ld_k + (int64_t)(hd - p.n_q) * 128;
+    uint2* xp = reinterpret_cast<uint2*>(base) + lane;
     const uint2 xv = *xp;
     float x[4] = {bf16_lo(xv.x), bf16_hi(xv.x), bf16_lo(xv.y), bf16_hi(xv.y)};
     float ss = 0.f;

@@ -458,27 +458,31 @@ int tg_add_rmsnorm(const void* h_in, int64_t ld_h_in, const void* delta, int64_t
   return TG_OK;
 }
 
-int tg_qk_norm_rope(void* qkv, int64_t rows, int64_t ld_row, int n_q_heads, int n_k_heads, int seq,
-                    const void* q_norm_w, const void* k_norm_w, const void* cos, const void* sin,
-                    int64_t cs_sb, int64_t cs_ss, int head_dim, float eps, void* stream) {
-  if (qkv == nullptr || q_norm_w == nullptr || k_norm_w == nullptr || cos == nullptr || sin == nullptr)
+int tg_qk_norm_rope(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k, int n_k_heads,
+                    int64_t rows, int seq, const void* q_norm_w, const void* k_norm_w,
+                    const void* cos, const void* sin, int64_t cs_sb, int64_t cs_ss, int head_dim,
+                    float eps, void* stream) {
+  if (q == nullptr || k == nullptr || q_norm_w == nullptr || k_norm_w == nullptr || cos == nullptr ||
+      sin == nullptr)
     return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope: NULL argument");
   if (head_dim != 128) return fail(TG_ERR_UNSUPPORTED, "qk_norm_rope: head_dim %d (only 128)", head_dim);
   if (rows < 0 || n_q_heads < 0 || n_k_heads < 0 || seq < 1 || (rows % seq) != 0)
     return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope: rows %lld must be a multiple of seq %d",
                 (long long)rows, seq);
-  if (ld_row < (int64_t)(n_q_heads + n_k_heads) * 128)
-    return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope: row stride shorter than the q and k heads");
-  const uintptr_t m = reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(q_norm_w) |
-                      reinterpret_cast<uintptr_t>(k_norm_w) | reinterpret_cast<uintptr_t>(cos) |
-                      reinterpret_cast<uintptr_t>(sin);
-  if ((m & 15) || ((ld_row | cs_sb | cs_ss) & 7))
+  if (ld_q < (int64_t)n_q_heads * 128 || ld_k < (int64_t)n_k_heads * 128)
+    return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope: row strides shorter than the heads");
+  const uintptr_t m = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                      reinterpret_cast<uintptr_t>(q_norm_w) | reinterpret_cast<uintptr_t>(k_norm_w) |
+                      reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin);
+  if ((m & 15) || ((ld_q | ld_k | cs_sb | cs_ss) & 7))
     return fail(TG_ERR_ALIGNMENT, "qk_norm_rope: pointers 16-byte aligned, strides multiples of 8 needed");
   if (rows == 0 || n_q_heads + n_k_heads == 0) return TG_OK;
   tg::QkRopeParams p;
-  p.qkv = static_cast<__nv_bfloat16*>(qkv);
+  p.q = static_cast<__nv_bfloat16*>(q);
+  p.k = static_cast<__nv_bfloat16*>(k);
   p.rows = rows;
-  p.ld_row = ld_row;
+  p.ld_q = ld_q;
+  p.ld_k = ld_k;
   p.n_q = n_q_heads;
   p.n_k = n_k_heads;
   p.seq = seq;

@@ -335,18 +335,22 @@ def add_rmsnorm(h: torch.Tensor, delta: Optional[torch.Tensor], weight: Optional
     return h_out, x
 
 
-def qk_norm_rope(qkv: torch.Tensor, n_q: int, n_k: int, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
+def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
                  cos: torch.Tensor, sin: torch.Tensor, eps: float) -> None:
-    """In place on qkv (B, S, heads, 128): RMS-norm + RoPE of the first n_q (q) and next n_k (k) heads.
+    """In place: RMS-norm + RoPE of every head of q (B, S, Hq, 128) and k (B, S, Hkv, 128).
 
-    cos/sin: (B, S, 128) bf16 (the rotary embedding of the rows' positions).
+    Heads must be contiguous 128-element rows; cos/sin: (B, S, 128) bf16 (the
+    rotary embedding of the rows' positions).
     """
-    _require_cuda("qkv", qkv, torch.bfloat16)
-    if qkv.dim() != 4 or qkv.shape[-1] != 128 or qkv.stride(-1) != 1 or qkv.stride(-2) != 128:
-        raise ValueError("qkv must be (B, S, heads, 128) with contiguous heads")
-    B, S = qkv.shape[0], qkv.shape[1]
-    if qkv.stride(0) != S * qkv.stride(1):
-        raise ValueError("qkv rows must be evenly strided across the batch")
+    for nm, t in (("q", q), ("k", k)):
+        _require_cuda(nm, t, torch.bfloat16)
+        if t.dim() != 4 or t.shape[-1] != 128 or t.stride(-1) != 1 or t.stride(-2) != 128:
+            raise ValueError(f"{nm} must be (B, S, heads, 128) with contiguous heads")
+        if t.stride(0) != t.shape[1] * t.stride(1):
+            raise ValueError(f"{nm} rows must be evenly strided across the batch")
+    B, S = q.shape[0], q.shape[1]
+    if k.shape[:2] != q.shape[:2]:
+        raise ValueError("q and k must cover the same rows")
     for nm, t in (("cos", cos), ("sin", sin)):
         _require_cuda(nm, t, torch.bfloat16)
         if t.shape != (B, S, 128) or t.stride(-1) != 1:
@@ -354,11 +358,11 @@ def qk_norm_rope(qkv: torch.Tensor, n_q: int, n_k: int, q_norm_w: torch.Tensor, 
     if cos.stride() != sin.stride():
         raise ValueError("cos and sin must share strides")
     L = _lib.lib()
-    with _device_ctx(qkv):
-        _lib.check(L.tg_qk_norm_rope(qkv.data_ptr(), B * S, qkv.stride(1), int(n_q), int(n_k), S,
-                                     q_norm_w.data_ptr(), k_norm_w.data_ptr(), cos.data_ptr(),
-                                     sin.data_ptr(), cos.stride(0), cos.stride(1), 128, float(eps),
-                                     _stream(qkv)))
+    with _device_ctx(q):
+        _lib.check(L.tg_qk_norm_rope(q.data_ptr(), q.stride(1), q.shape[2], k.data_ptr(), k.stride(1),
+                                     k.shape[2], B * S, S, q_norm_w.data_ptr(), k_norm_w.data_ptr(),
+                                     cos.data_ptr(), sin.data_ptr(), cos.stride(0), cos.stride(1), 128,
+                                     float(eps), _stream(q)))
 
 
 def silu_mul(gu: torch.Tensor) -> torch.Tensor:

@@ -46,6 +46,13 @@ def _ids_to_device(prompt_ids_list, device) -> torch.Tensor:
     B = len(prompt_ids_list)
     if B == 1 and torch.is_tensor(prompt_ids_list[0]):
         return prompt_ids_list[0].to(device=device, dtype=torch.long, non_blocking=True).reshape(1, -1)
+    if all(torch.is_tensor(x) and x.device == torch.device(device) for x in prompt_ids_list):
+        # ids already on the GPU (a serving loop's tokens): right-pad there
+        lens = [int(x.numel()) for x in prompt_ids_list]
+        out = torch.zeros(B, max(lens), dtype=torch.long, device=device)
+        for b, x in enumerate(prompt_ids_list):
+            out[b, :lens[b]] = x.reshape(-1)
+        return out
     lens = [len(x) for x in prompt_ids_list]
     host = torch.zeros(B, max(lens), dtype=torch.long, pin_memory=torch.cuda.is_available())
     for b, ids in enumerate(prompt_ids_list):
