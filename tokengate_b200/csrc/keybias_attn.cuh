@@ -22,8 +22,7 @@
 //  * warps 0-3 / 4-7 are the softmax warpgroups of tile 0 / tile 1: one TMEM
 //    lane (= one query row) per thread, the 128-key row in registers, a
 //    3-input max over the raw logits, p = 2^(S*scale*log2e - m) with one
-//    packed FFMA2 per pair, exp2 on the MUFU for three of every four pairs
-//    and on the FMA pipe (polynomial) for the fourth. The running max is only
+//    packed FFMA2 per pair and exp2 on the MUFU. The running max is only
 //    moved (and O rescaled in TMEM) when it grows by more than 2^8, so
 //    rescales are rare; numerator and denominator share the stale max, so
 //    the result is exact.
@@ -491,8 +490,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float msub = (m_run == -INFINITY) ? 0.f : m_run;
       const float2 negm = make_float2(-msub, -msub);
 
-      // p = 2^(S*c2 - m): one FFMA2 per pair; three of every four pairs on
-      // the MUFU, one on the FMA pipe; packed bf16 pairs in two halves
+      // p = 2^(S*c2 - m): one FFMA2 per pair, exp2 on the MUFU (measured
+      // faster here than moving a share of the pairs to an FMA-pipe
+      // polynomial); packed bf16 pairs written in two halves
       float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -503,12 +503,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const float2 d = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
                                       c22, negm);
           float2 pp;
-          if ((q & 3) == 3) {
-            pp = exp2_poly2(d);
-          } else {
-            pp.x = ex2_approx(d.x);
-            pp.y = ex2_approx(d.y);
-          }
+          pp.x = ex2_approx(d.x);
+          pp.y = ex2_approx(d.y);
           if (q & 1) ls1 = __fadd2_rn(ls1, pp); else ls0 = __fadd2_rn(ls0, pp);
           pk[q] = pack_bf16x2(pp.x, pp.y);
         }
