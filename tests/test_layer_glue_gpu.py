@@ -19,11 +19,16 @@ from tokengate_b200 import prefill as tgp
 pytestmark = pytest.mark.gpu
 
 
-def _close_bf16(got, ref, min_exact=0.99):
+def _close_bf16(got, ref, min_exact=0.99, atol=0.0):
+    """|got - ref| <= 2^-7 |ref| + atol everywhere, and >= min_exact bit-identical.
+
+    atol covers outputs formed by cancellation (RoPE: y*cos + rot(y)*sin), where
+    one ulp of an O(1) intermediate is a large relative error on a small result.
+    """
     g, r = got.float(), ref.float()
-    rel = ((g - r).abs() / r.abs().clamp_min(1e-6)).max().item()
+    excess = ((g - r).abs() - (2 ** -7 * r.abs() + atol)).max().item()
     exact = (got.view(torch.int16) == ref.view(torch.int16)).float().mean().item()
-    assert rel <= 2 ** -7 or (g - r).abs().max().item() < 1e-6, f"max rel {rel}"
+    assert excess <= 0.0, f"exceeds the bound by {excess}"
     assert exact >= min_exact, f"only {exact:.4f} bit-identical"
 
 
@@ -70,8 +75,9 @@ def test_qk_norm_rope(cuda):
                                             kn(qkv[:, :, nq:nq + nkv]).transpose(1, 2), cos, sin)
     got = qkv.clone()
     ops.qk_norm_rope(got[:, :, :nq], got[:, :, nq:nq + nkv], qn.weight, kn.weight, cos, sin, 1e-6)
-    _close_bf16(got[:, :, :nq], q_ref.transpose(1, 2))
-    _close_bf16(got[:, :, nq:nq + nkv], k_ref.transpose(1, 2))
+    # one bf16 ulp of the O(1) normalised intermediate (2^-7) as the absolute term
+    _close_bf16(got[:, :, :nq], q_ref.transpose(1, 2), atol=2 ** -7)
+    _close_bf16(got[:, :, nq:nq + nkv], k_ref.transpose(1, 2), atol=2 ** -7)
     assert torch.equal(got[:, :, nq + nkv:], qkv[:, :, nq + nkv:])   # v untouched
     # separate q and k buffers
     q2, k2 = qkv[:, :, :nq].contiguous(), qkv[:, :, nq:nq + nkv].contiguous()

@@ -118,47 +118,80 @@ struct QkRopeParams {
   float eps;
 };
 
-// one warp per (row, head); lane l holds elements 4l..4l+3, its rotate-half
-// partner elements (d +- 64) live in lane l ^ 16
-__global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkRopeParams p) {
-  const int lane = threadIdx.x & 31;
+// One half-warp per (row, head): lane l of the half holds elements 8l..8l+7
+// (16-byte loads), its rotate-half partner elements (d +- 64) live in lane
+// l ^ 8; each half-warp keeps two heads in flight per iteration.
+__device__ __forceinline__ void qk_head(const QkRopeParams& p, int64_t item, int hl, bool active) {
   const int heads = p.n_q + p.n_k;
-  const int64_t total = p.rows * heads;
-  const int64_t warp_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t wi = warp_global; wi < total; wi += n_warps) {
-    const int64_t row = wi / heads;
-    const int hd = (int)(wi - row * heads);
-    const bool is_q = hd < p.n_q;
-    const __nv_bfloat16* w = is_q ? p.q_w : p.k_w;
-    __nv_bfloat16* base = is_q ? p.q + row * p.ld_q + (int64_t)hd * 128
-                               : p.k + row * p.ld_k + (int64_t)(hd - p.n_q) * 128;
-    uint2* xp = reinterpret_cast<uint2*>(base) + lane;
-    const uint2 xv = *xp;
-    float x[4] = {bf16_lo(xv.x), bf16_hi(xv.x), bf16_lo(xv.y), bf16_hi(xv.y)};
-    float ss = 0.f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) ss = fmaf(x[e], x[e], ss);
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss * (1.f / 128.f) + p.eps);
-    const uint2 wv = __ldg(reinterpret_cast<const uint2*>(w) + lane);
-    const float wf[4] = {bf16_lo(wv.x), bf16_hi(wv.x), bf16_lo(wv.y), bf16_hi(wv.y)};
-    float y[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) y[e] = round_bf16(wf[e] * round_bf16(x[e] * inv));
+  const int64_t row = item / heads;
+  const int hd = (int)(item - row * heads);
+  const bool is_q = hd < p.n_q;
+  const __nv_bfloat16* w = is_q ? p.q_w : p.k_w;
+  __nv_bfloat16* base = is_q ? p.q + row * p.ld_q + (int64_t)hd * 128
+                             : p.k + row * p.ld_k + (int64_t)(hd - p.n_q) * 128;
+  uint4* xp = reinterpret_cast<uint4*>(base) + hl;
+  uint4 xv = make_uint4(0u, 0u, 0u, 0u), cv = xv, sv = xv, wv = xv;
+  if (active) {
     const int64_t b = row / p.seq, s = row - b * p.seq;
-    const uint2 cv = __ldg(reinterpret_cast<const uint2*>(p.cos + b * p.cs_sb + s * p.cs_ss) + lane);
-    const uint2 sv = __ldg(reinterpret_cast<const uint2*>(p.sin + b * p.cs_sb + s * p.cs_ss) + lane);
-    const float cf[4] = {bf16_lo(cv.x), bf16_hi(cv.x), bf16_lo(cv.y), bf16_hi(cv.y)};
-    const float sf[4] = {bf16_lo(sv.x), bf16_hi(sv.x), bf16_lo(sv.y), bf16_hi(sv.y)};
-    float o[4];
+    xv = *xp;
+    wv = __ldg(reinterpret_cast<const uint4*>(w) + hl);
+    cv = __ldg(reinterpret_cast<const uint4*>(p.cos + b * p.cs_sb + s * p.cs_ss) + hl);
+    sv = __ldg(reinterpret_cast<const uint4*>(p.sin + b * p.cs_sb + s * p.cs_ss) + hl);
+  }
+  const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
+  float x[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
-      const float rot = lane < 16 ? -partner : partner;   // rotate_half: [-x2, x1]
-      o[e] = round_bf16(round_bf16(y[e] * cf[e]) + round_bf16(rot * sf[e]));
+  for (int e = 0; e < 4; ++e) {
+    x[2 * e] = bf16_lo(xw[e]);
+    x[2 * e + 1] = bf16_hi(xw[e]);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+#pragma unroll
+  for (int off = 8; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);  // within the half
+  const float inv = rsqrtf(ss * (1.f / 128.f) + p.eps);
+  const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
+  const uint32_t* cw = reinterpret_cast<const uint32_t*>(&cv);
+  const uint32_t* sw = reinterpret_cast<const uint32_t*>(&sv);
+  float y[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    y[2 * e] = round_bf16(bf16_lo(ww[e]) * round_bf16(x[2 * e] * inv));
+    y[2 * e + 1] = round_bf16(bf16_hi(ww[e]) * round_bf16(x[2 * e + 1] * inv));
+  }
+  uint4 ov;
+  uint32_t* ow = reinterpret_cast<uint32_t*>(&ov);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float o2[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const float yy = y[2 * e + u];
+      const float partner = __shfl_xor_sync(0xffffffffu, yy, 8);
+      const float rot = hl < 8 ? -partner : partner;   // rotate_half: [-x2, x1]
+      const float c = u ? bf16_hi(cw[e]) : bf16_lo(cw[e]);
+      const float sn = u ? bf16_hi(sw[e]) : bf16_lo(sw[e]);
+      o2[u] = round_bf16(round_bf16(yy * c) + round_bf16(rot * sn));
     }
-    *xp = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+    ow[e] = pack_bf16x2(o2[0], o2[1]);
+  }
+  if (active) *xp = ov;
+}
+
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkRopeParams p) {
+  const int hl = threadIdx.x & 15;  // lane inside the half-warp
+  const int64_t total = p.rows * (p.n_q + p.n_k);
+  const int64_t half_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int64_t n_halves = ((int64_t)gridDim.x * blockDim.x) >> 4;
+  // two items per iteration; the loop bound is uniform across the warp
+  // (both halves iterate until every half of the warp is done)
+  const int64_t warp_first = half_global & ~int64_t(1);
+  for (int64_t base = warp_first; base < total; base += 2 * n_halves) {
+    const int64_t i0 = base + (half_global & 1);
+    const int64_t i1 = i0 + n_halves;
+    qk_head(p, i0, hl, i0 < total);
+    qk_head(p, i1, hl, i1 < total);
   }
 }
 
