@@ -29,6 +29,10 @@ Reported (one JSON line from rank 0):
   --impl reference times that CPU implementation alone (rank 0), the
   reference arm: the reference's path is Python and CUDA code that cannot be
   built or shipped to the GPU box, so its CPU restatement stands in for it.
+  --gate e2e runs the same workload with the finalized gate instead of the
+  synthetic linear one (a seeded E2EGate: SwiGLU scoring branch cloned from
+  layer 1, per-layer per-head bias, scaled-softmax query scale); the default
+  is BASELINE's linear gate.
 """
 import argparse
 import json
@@ -123,7 +127,7 @@ class KernelMeter:
         self.ops = ops
         self.orig = {n: getattr(ops, n) for n in ("keybias_attention", "gate_score", "topk_select",
                                                   "gather_rows", "add_rmsnorm", "qk_norm_rope",
-                                                  "silu_mul")}
+                                                  "silu_mul", "branch_score", "phase2_tables")}
         self.active = False
         self.launches = 0
         self.attn = []   # (flops, start_event, end_event)
@@ -164,6 +168,8 @@ class KernelMeter:
         ops.add_rmsnorm = counted("add_rmsnorm", lambda a, kw: 1)
         ops.qk_norm_rope = counted("qk_norm_rope", lambda a, kw: 1)
         ops.silu_mul = counted("silu_mul", lambda a, kw: 1)
+        ops.branch_score = counted("branch_score", lambda a, kw: (a[0].shape[0] + 127) // 128)
+        ops.phase2_tables = counted("phase2_tables", lambda a, kw: (a[3].shape[0] + 127) // 128)
 
     def attention_summary(self):
         flops = sum(f for f, _, _ in self.attn)
@@ -171,9 +177,10 @@ class KernelMeter:
         return flops, ms, len(self.attn)
 
 
-def build_model(device):
+def build_model(device, gate_kind="linear"):
     from tokengate_b200.inference import load_model
-    return load_model(base_model=MODEL, gate_layer=GATE_LAYER, gate_attn="b200", device=device, seed=0)
+    return load_model(base_model=MODEL, gate_layer=GATE_LAYER, gate_attn="b200", device=device, seed=0,
+                      gate="e2e" if gate_kind == "e2e" else None)
 
 
 def make_prompt(seed: int, n: int, vocab: int) -> torch.Tensor:
@@ -188,14 +195,29 @@ def cpu_oracle_sample(tm, steps: int, warmup: int):
     torch.set_num_threads(threads)
     cpu_model = tm.model
     weights = opre.weights_fp32(cpu_model)
-    w = tm.gate.readout.weight.detach().cpu()
     c = CPU_SAMPLE
     ids = make_prompt(1234, c["seq_len"], tm.model.config.vocab_size).tolist()
+    if getattr(tm.gate, "gate_branch", None) is not None:
+        br, gt = tm.gate.gate_branch, tm.gate
+        gp = dict(wg=br.gate_proj.weight.detach().cpu(), wu=br.up_proj.weight.detach().cpu(),
+                  w_row=br.down_proj.weight.detach().cpu()[0],
+                  gate_scale_eff=torch.nn.functional.softplus(gt.gate_scale.detach().cpu()),
+                  attn_scale_eff=torch.nn.functional.softplus(gt.attn_scale.detach().cpu()),
+                  eps=float(gt.b_norm.variance_epsilon), gain=float(gt.b_norm.weight.detach().cpu()[0]))
+
+        def run():
+            opre.gated_prefill_e2e(cpu_model, gp, [ids], [c["state_begin"]], [c["state_end"]], GATE_LAYER,
+                                   c["K"], weights=weights)
+    else:
+        w = tm.gate.readout.weight.detach().cpu()
+
+        def run():
+            opre.gated_prefill(cpu_model, w, [ids], [c["state_begin"]], [c["state_end"]], GATE_LAYER, c["K"],
+                               weights=weights, bias_bf16=True)
     times = []
     for i in range(warmup + steps):
         t0 = time.perf_counter()
-        opre.gated_prefill(cpu_model, w, [ids], [c["state_begin"]], [c["state_end"]], GATE_LAYER, c["K"],
-                           weights=weights, bias_bf16=True)
+        run()
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)
@@ -246,6 +268,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gate", default="linear", choices=("linear", "e2e"),
+                    help="linear: BASELINE's synthetic gate; e2e: a seeded finalized gate (E2EGate)")
     ap.add_argument("--profile-step", action="store_true",
                     help="after the warm-up, run ONE step between cudaProfilerStart/Stop and exit "
                          "(for ncu --profile-from-start off); prints no bench line")
@@ -268,7 +292,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
         pg = dist
 
-    tm = build_model(dev)
+    tm = build_model(dev, args.gate)
     vocab = tm.model.config.vocab_size
     prompt = make_prompt(1000 + rank, SEQ_LEN, vocab)
     ids_dev = prompt.to(dev)
@@ -352,15 +376,17 @@ def main():
 
     peaks = _peaks()
     achieved = a_flops / (a_ms / 1e3) / 1e12 if a_ms > 0 else None
+    metric = METRIC if args.gate == "linear" else METRIC[:-1] + ", finalized gate)"
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "ttft_ms": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (uniform random ids, random-init weights)",
         "config": {"workload": "BASELINE config 3: Qwen3-1.7B-shape gated prefill, 32768-token prompt, "
                                "state [512, 32512), K=2000, gate layer 1",
                    "model": MODEL, "global_batch": world, "seq_len": SEQ_LEN, "K": K_KEEP,
-                   "gate_layer": GATE_LAYER, "parallelism": f"request replicas x{world}",
+                   "gate_layer": GATE_LAYER, "gate": args.gate,
+                   "parallelism": f"request replicas x{world}",
                    "l2": "working set > L2 (3.4 GB weights, ~1 GB activations per step); no flush"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s / args.steps * 1e3},

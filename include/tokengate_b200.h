@@ -204,6 +204,61 @@ int tg_qk_norm_rope(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k,
 int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_t rows, int64_t inter,
                 void* stream);
 
+/*
+ * a4 (finalized gate) — readout of the scoring branch:
+ *   score[b, r] = bf16( sum_k bf16(bf16(silu(g_k)) * u_k) * w[k] ),  stored as fp32
+ * over the fused [gate | up] projection row GU[b, row_begin[b] + r] = [g | u]
+ * of the LN2-normalised gate-layer boundary, for r < row_count[b].
+ *
+ * Replaces the scoring branch of the finalized E2EGate,
+ *   gate_branch_hs -> br(z) with the absorbed 1-row down_proj
+ *   (tokengate/e2e_gate/gate_module/gate_forward.py:491-524, :330-340),
+ *   computed in bf16 by CastLinear (e2e_gate_module.py:125-135) and returned
+ *   as bf16 (gate_forward.py:521), then cast to the gate's fp32 (:1402-1405).
+ * The dot product has a fixed order and silu uses IEEE operations only, so the
+ * result is reproducible bit for bit; -0 is stored as +0.
+ *
+ * gu: bf16 (B, S, >= 2*inter), strides (gu_sb, gu_ss, 1), rows 16-byte aligned;
+ * inter a multiple of 256. w_row: bf16 (inter,), 16-byte aligned.
+ * row_begin / row_count: HOST arrays of B ints. scores: fp32, batch stride s_sb.
+ */
+int tg_branch_score(const void* gu, int64_t gu_sb, int64_t gu_ss, int inter, const void* w_row,
+                    int B, const int32_t* row_begin, const int32_t* row_count, float* scores,
+                    int64_t s_sb, void* stream);
+
+/*
+ * a5 + a9 + a2 (finalized gate) — the Phase-2 operands of every biased layer
+ * from the raw branch scores, in one launch. For request b, kept slot t
+ * (position p = keep[b, t]), Phase-2 layer l and head h:
+ *   rs      = rsqrt(mean over the state span of score^2 + eps)
+ *   b       = bf16(gain * (score[p - state_begin] * rs) * gate_scale[l, h])  (state tokens)
+ *   r       = bf16(min(log(max(t + 1, 2)) / log(max(p + 1, 2)), 1))
+ *   q_scale[l, b, h, t] = s = bf16(bf16(attn_scale[l, h]) * r)
+ *   bias[l, b, h, t]    = bf16(x * bf16(mean_h s)),  x = b on kept state tokens,
+ *                         0 on kept non-state tokens, bf16(-1e9) for t >= n_kept[b]
+ * gate_scale / attn_scale are the EFFECTIVE (softplus-applied) (L', H) fp32 tables.
+ *
+ * Replaces E2EGate.forward's sequence RMSNorm x softplus(gate_scale)
+ *   (tokengate/e2e_gate/gate_module/e2e_gate_module.py:327-385),
+ *   build_gate_bias_vectorized + the -1e9 pads (gate_forward.py:968-1000,
+ *   :1463-1469), _ssmax_ratio (:574-585), the per-layer slicing of
+ *   _apply_gate_bias (:588-660) and the scaled-softmax prologue
+ *   _ssmax_s_eff / _phase2_q_bias (tokengate/e2e_gate/attn/
+ *   qwen3_flex_attention.py:417-473).
+ *
+ * scores: fp32 (B, >= n_state[b]), batch stride s_sb, state token i at i.
+ * keep: int64 (B, >= n_alloc), batch stride keep_sb (pads included).
+ * state_begin / n_state / n_kept: HOST arrays of B ints.
+ * bias / q_scale: fp32 (n_layers, B, n_heads, n_alloc), contiguous; layer l's
+ * slice is the (B, H, S) bias / q_row_scale operand of tg_keybias_attn_fwd.
+ * n_layers * n_heads <= 4096.
+ */
+int tg_phase2_tables(const float* scores, int64_t s_sb, int B, const int32_t* state_begin,
+                     const int32_t* n_state, const int64_t* keep, int64_t keep_sb,
+                     const int32_t* n_kept, int n_alloc, const float* gate_scale,
+                     const float* attn_scale, int n_layers, int n_heads, float eps, float gain,
+                     float* bias, float* q_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,27 +41,34 @@ def _rot_half(x):
     return torch.cat([-x[..., h:], x[..., :h]], dim=-1)
 
 
-def _attention(q, k, v, bias_bs, chunk=256):
-    """q (B,S,Hq,D), k/v (B,S,Hkv,D) fp32, bias_bs (B,S) or None; causal."""
+def _attention(q, k, v, bias_bs, chunk=256, q_scale=None):
+    """q (B,S,Hq,D), k/v (B,S,Hkv,D) fp32, bias_bs (B,S) or (B,Hq,S) or None; causal.
+    q_scale (B,Hq|1,S) multiplies each query row (the scaled-softmax prologue)."""
     B, S, Hq, D = q.shape
     G = Hq // k.shape[2]
     kk = k.repeat_interleave(G, dim=2).permute(0, 2, 3, 1)     # (B, Hq, D, S)
     vv = v.repeat_interleave(G, dim=2).permute(0, 2, 1, 3)     # (B, Hq, S, D)
     qq = q.permute(0, 2, 1, 3)                                 # (B, Hq, S, D)
+    if q_scale is not None:
+        qq = qq * q_scale[..., None]
     out = torch.empty_like(qq)
     keys = torch.arange(S)
     for c0 in range(0, S, chunk):
         c1 = min(S, c0 + chunk)
         s = (qq[:, :, c0:c1] @ kk) * (D ** -0.5)
         if bias_bs is not None:
-            s = s + bias_bs[:, None, None, :]
+            s = s + (bias_bs[:, None, None, :] if bias_bs.dim() == 2 else bias_bs[:, :, None, :])
         s = s.masked_fill(keys[None, None, None, :] > torch.arange(c0, c1)[None, None, :, None],
                           float("-inf"))
         out[:, :, c0:c1] = torch.softmax(s, dim=-1) @ vv
     return out.permute(0, 2, 1, 3)
 
 
-def _layer(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs):
+def _layer(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs, q_scale=None):
+    return _mlp_half(_attn_half(h, p, cfg, cos, sin, bias_bs, q_scale), p, cfg)
+
+
+def _attn_half(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs, q_scale=None):
     B, S, _ = h.shape
     D = cfg["head_dim"]
     eps = cfg["rms_norm_eps"]
@@ -74,8 +81,12 @@ def _layer(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs):
     c, s_ = cos[:, :, None, :], sin[:, :, None, :]
     q = q * c + _rot_half(q) * s_
     k = k * c + _rot_half(k) * s_
-    a = _attention(q, k, v, bias_bs).reshape(B, S, -1)
-    h = h + a @ p["self_attn.o_proj.weight"].T
+    a = _attention(q, k, v, bias_bs, q_scale=q_scale).reshape(B, S, -1)
+    return h + a @ p["self_attn.o_proj.weight"].T
+
+
+def _mlp_half(h, p: Dict[str, torch.Tensor], cfg):
+    eps = cfg["rms_norm_eps"]
     x = _rms(h, p["post_attention_layernorm.weight"], eps)
     g = x @ p["mlp.gate_proj.weight"].T
     u = x @ p["mlp.up_proj.weight"].T
@@ -153,3 +164,77 @@ def gated_prefill(model, w_gate: torch.Tensor, prompt_ids_list: Sequence[Sequenc
     return dict(first_tokens=logits.argmax(-1), kept_positions=[k.tolist() for k in kept],
                 n_kepts=n_kepts, K_clampeds=K_cl, logits=logits, scores=scores,
                 phase1_hidden=phase1_hidden, bias=bias)
+
+
+def gated_prefill_e2e(model, gate: dict, prompt_ids_list: Sequence[Sequence[int]],
+                      starts: Sequence[int], ends: Sequence[int], gate_layer: int, K,
+                      weights=None) -> dict:
+    """The gated prefill with the finalized gate, float32 on the CPU.
+
+    gate: dict(wg (inter, H), wu (inter, H), w_row (inter,), gate_scale_eff (L', Hg),
+    attn_scale_eff (L', Hg), eps, gain) — fp32 tensors/arrays. Restates the split
+    gate layer (attention half in Phase 1, gate_forward.py:345-418; its MLP on the
+    kept rows at Phase-2 entry, :420-435, :1481-1483), the branch score
+    (:491-524), E2EGate.forward / aggregate (e2e_gate_module.py:348-399), the
+    selection on the aggregate, the per-layer per-head bias and the
+    scaled-softmax query scale of every Phase-2 layer (:588-660,
+    qwen3_flex_attention.py:417-473) in float32 arithmetic.
+    Returns dict(first_tokens, kept_positions, n_kepts, K_clampeds, logits, raw_scores).
+    """
+    import numpy as np
+    from . import gate_e2e as ge
+    layers, g, cfg = weights if weights is not None else weights_fp32(model)
+    B = len(prompt_ids_list)
+    lens = [len(x) for x in prompt_ids_list]
+    S = max(lens)
+    ids = torch.zeros(B, S, dtype=torch.long)
+    for b, x in enumerate(prompt_ids_list):
+        ids[b, :lens[b]] = torch.as_tensor(list(x), dtype=torch.long)
+    h = g["embed"][ids]
+    pos = torch.arange(S).unsqueeze(0).expand(B, -1)
+    cos, sin = _rope_cos_sin(pos, cfg["head_dim"], cfg["rope_theta"])
+    for i in range(gate_layer):
+        h = _layer(h, layers[i], cfg, cos, sin, None)
+    h = _attn_half(h, layers[gate_layer], cfg, cos, sin, None)          # a_j
+    z = _rms(h, layers[gate_layer]["post_attention_layernorm.weight"], cfg["rms_norm_eps"])
+    wg, wu, w_row = (torch.as_tensor(np.asarray(gate[k]), dtype=torch.float32) for k in ("wg", "wu", "w_row"))
+    gs = np.asarray(gate["gate_scale_eff"], dtype=np.float32)
+    at = torch.as_tensor(np.asarray(gate["attn_scale_eff"], dtype=np.float32))
+    Ks = list(K) if isinstance(K, (list, tuple)) else [K] * B
+    kept, raws, bs, n_kepts, K_cl = [], [], [], [], []
+    for b in range(B):
+        zb = z[b, starts[b]:ends[b]]
+        raw = ((torch.nn.functional.silu(zb @ wg.T) * (zb @ wu.T)) @ w_row).numpy()
+        bb = ge.e2e_bias(raw, gs, gate["eps"], gate["gain"])                 # (n, L', Hg)
+        kc = max(1, min(int(Ks[b]), len(raw)))
+        top = torch.as_tensor(ge.select(ge.aggregate(bb), kc), dtype=torch.long)
+        keep = torch.cat([torch.arange(starts[b]), starts[b] + top, torch.arange(ends[b], lens[b])])
+        kept.append(keep)
+        raws.append(raw)
+        bs.append(bb)
+        n_kepts.append(len(keep))
+        K_cl.append(kc)
+    n_alloc = max(n_kepts)
+    Lp, Hg = gs.shape
+    hp = torch.zeros(B, n_alloc, h.shape[-1])
+    kp = torch.zeros(B, n_alloc, dtype=torch.long)
+    base = torch.zeros(B, n_alloc, Lp, Hg)
+    for b in range(B):
+        n = n_kepts[b]
+        hp[b, :n] = h[b, kept[b]]
+        kp[b, :n] = kept[b]
+        st = kept[b][starts[b]:starts[b] + K_cl[b]] - starts[b]
+        base[b, starts[b]:starts[b] + K_cl[b]] = torch.as_tensor(bs[b])[st]
+        base[b, n:] = -1e9
+    hp = _mlp_half(hp, layers[gate_layer], cfg)                         # gate layer MLP on kept rows
+    r = torch.as_tensor(ge.ssmax_ratio(kp.numpy()))                     # (B, n_alloc)
+    cos2, sin2 = _rope_cos_sin(kp, cfg["head_dim"], cfg["rope_theta"])
+    for li, i in enumerate(range(gate_layer + 1, cfg["n_layers"])):
+        s_eff = at[li].view(1, -1, 1) * r[:, None, :]                   # (B, Hg, n)
+        sb = s_eff.mean(dim=1)                                          # (B, n)
+        bias = (base[:, :, li, :] * sb[:, :, None]).permute(0, 2, 1)    # (B, Hg, n)
+        hp = _layer(hp, layers[i], cfg, cos2, sin2, bias, q_scale=s_eff)
+    last = torch.stack([_rms(hp[b, n_kepts[b] - 1], g["norm"], cfg["rms_norm_eps"]) for b in range(B)])
+    logits = last @ g["lm_head"].T
+    return dict(first_tokens=logits.argmax(-1), kept_positions=[k.tolist() for k in kept],
+                n_kepts=n_kepts, K_clampeds=K_cl, logits=logits, raw_scores=raws)

@@ -13,7 +13,13 @@
  *                        the log-sigmoid BASELINE's config 2 names);
  *   oracle_topk_select  torch.topk + keep-list + Phase-2 bias row
  *                       (gate_forward.py:84-99, :1409-1421, :968-1036, :1463-1469),
- *                       ordering (score desc, index asc).
+ *                       ordering (score desc, index asc);
+ *   oracle_branch_score the finalized gate's scoring-branch readout
+ *                       bf16(sum_k bf16(bf16(silu(g_k)) * u_k) * w_k) over a
+ *                       fused [gate | up] row (gate_branch_hs,
+ *                       gate_forward.py:491-524, absorbed 1-row down_proj
+ *                       :330-340, Qwen3MLP rounding points), in the kernel's
+ *                       fixed order, silu with the IEEE-only exp below.
  *
  * The scorer fixes one summation order (documented in the kernel source):
  * 32 lane partials, lane l summing elements 8*(l+32*i)+e for i, e ascending
@@ -198,4 +204,76 @@ int64_t oracle_topk_select(const float* scores, int n_state, int k, int state_be
   free(ki);
   free(sel);
   return n_kept;
+}
+
+
+/* ---------------------------------------------------------------- finalized gate */
+
+/* bf16 round-to-nearest-even of a finite fp32 value, returned as fp32 */
+static float bf16_round(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) return x; /* inf / nan pass through */
+  u += 0x7fffu + ((u >> 16) & 1u);
+  u &= 0xffff0000u;
+  return u32_as_f32(u);
+}
+
+/* exp(y): y = k ln2 + r, |r| <= ln2/2, degree-7 Taylor for exp(r), 2^k in two
+ * exact steps; 0 below -104, +inf above the largest finite result */
+static float exp_any(float y) {
+  if (y < -104.0f) return 0.0f;
+  if (y > 88.72283935546875f) return u32_as_f32(0x7f800000u);
+  const float kInvLn2 = 1.44269504088896341f;
+  const float kLn2Hi = 0.693145751953125f;
+  const float kLn2Lo = 1.42860682030941723212e-6f;
+  const float k = rintf(y * kInvLn2);
+  float r = fmaf(-k, kLn2Hi, y);
+  r = fmaf(-k, kLn2Lo, r);
+  float q = 1.98412698412698413e-4f;
+  q = fmaf(q, r, 1.38888888888888889e-3f);
+  q = fmaf(q, r, 8.33333333333333333e-3f);
+  q = fmaf(q, r, 4.16666666666666667e-2f);
+  q = fmaf(q, r, 1.66666666666666667e-1f);
+  q = fmaf(q, r, 0.5f);
+  q = fmaf(q, r, 1.0f);
+  q = fmaf(q, r, 1.0f);
+  const int ki = (int)k;
+  const int k1 = ki > 100 ? 100 : (ki < -100 ? -100 : ki);
+  const int k2 = ki - k1;
+  q = q * u32_as_f32((uint32_t)(127 + k1) << 23);
+  if (k2 != 0) q = q * u32_as_f32((uint32_t)(127 + k2) << 23);
+  return q;
+}
+
+float oracle_silu(float g) { return g / (1.0f + exp_any(-g)); }
+
+/* rows x [g (inter) | u (inter)] bf16 with row stride ld (elements); w: bf16 (inter,) */
+void oracle_branch_score(const uint16_t* gu, int64_t ld, int64_t rows, int inter, const uint16_t* w,
+                         float* out) {
+  const int nv = inter / 256;
+  for (int64_t r = 0; r < rows; ++r) {
+    const uint16_t* g = gu + r * ld;
+    const uint16_t* u = g + inter;
+    float part[32];
+    for (int lane = 0; lane < 32; ++lane) {
+      float acc = 0.0f;
+      for (int i = 0; i < nv; ++i) {
+        for (int e = 0; e < 8; ++e) {
+          const int k = 8 * (lane + 32 * i) + e;
+          const float s = bf16_round(oracle_silu(bf16_to_f32(g[k])));
+          const float a = bf16_round(s * bf16_to_f32(u[k]));
+          acc = fmaf(a, bf16_to_f32(w[k]), acc);
+        }
+      }
+      part[lane] = acc;
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+      float nxt[32];
+      for (int lane = 0; lane < 32; ++lane) nxt[lane] = part[lane] + part[lane ^ off];
+      memcpy(part, nxt, sizeof(part));
+    }
+    const float sc = bf16_round(part[0]);
+    out[r] = sc == 0.0f ? 0.0f : sc;
+  }
 }

@@ -17,6 +17,7 @@
 #include "topk_select.cuh"
 #include "gather_rows.cuh"
 #include "layer_glue.cuh"
+#include "e2e_gate.cuh"
 
 // Bit flags set by kernels whose bounded waits gave up (see ptx.cuh).
 __device__ unsigned int g_tg_device_error = 0;
@@ -519,6 +520,108 @@ int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_
   tg::silu_mul_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
+  return TG_OK;
+}
+
+int tg_branch_score(const void* gu, int64_t gu_sb, int64_t gu_ss, int inter, const void* w_row,
+                    int B, const int32_t* row_begin, const int32_t* row_count, float* scores,
+                    int64_t s_sb, void* stream) {
+  if (gu == nullptr || w_row == nullptr || scores == nullptr || row_begin == nullptr ||
+      row_count == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "branch_score: NULL argument");
+  if (B < 1) return fail(TG_ERR_INVALID_ARGUMENT, "branch_score: B=%d", B);
+  if (inter < 256 || inter % 256 != 0)
+    return fail(TG_ERR_UNSUPPORTED, "branch_score: inter %d must be a positive multiple of 256", inter);
+  if (gu_ss < 2 * (int64_t)inter)
+    return fail(TG_ERR_INVALID_ARGUMENT, "branch_score: row stride %lld shorter than 2*inter",
+                (long long)gu_ss);
+  if (((reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(w_row)) & 15) || (gu_ss & 7) ||
+      (gu_sb & 7))
+    return fail(TG_ERR_ALIGNMENT, "branch_score: rows and w_row must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int b0 = 0; b0 < B; b0 += tg::kBranchMaxReq) {
+    const int nb = B - b0 < tg::kBranchMaxReq ? B - b0 : tg::kBranchMaxReq;
+    tg::BranchParams p;
+    memset(&p, 0, sizeof(p));
+    p.gu = static_cast<const __nv_bfloat16*>(gu) + (int64_t)b0 * gu_sb;
+    p.gu_sb = gu_sb;
+    p.gu_ss = gu_ss;
+    p.inter = inter;
+    p.w = static_cast<const __nv_bfloat16*>(w_row);
+    p.out = scores + (int64_t)b0 * s_sb;
+    p.out_sb = s_sb;
+    p.B = nb;
+    p.row_off[0] = 0;
+    for (int i = 0; i < nb; ++i) {
+      if (row_begin[b0 + i] < 0 || row_count[b0 + i] < 0)
+        return fail(TG_ERR_INVALID_ARGUMENT, "branch_score: negative row range for request %d", b0 + i);
+      p.begin[i] = row_begin[b0 + i];
+      p.row_off[i + 1] = p.row_off[i] + row_count[b0 + i];
+    }
+    p.total_rows = p.row_off[nb];
+    if (p.total_rows == 0) continue;
+    const int64_t blocks = resident_blocks((p.total_rows + 7) / 8, 4);  // 62 registers: 4 CTAs per SM
+    tg::branch_score_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "branch_score launch");
+  }
+  return TG_OK;
+}
+
+int tg_phase2_tables(const float* scores, int64_t s_sb, int B, const int32_t* state_begin,
+                     const int32_t* n_state, const int64_t* keep, int64_t keep_sb,
+                     const int32_t* n_kept, int n_alloc, const float* gate_scale,
+                     const float* attn_scale, int n_layers, int n_heads, float eps, float gain,
+                     float* bias, float* q_scale, void* stream) {
+  if (scores == nullptr || state_begin == nullptr || n_state == nullptr || keep == nullptr ||
+      n_kept == nullptr || gate_scale == nullptr || attn_scale == nullptr || bias == nullptr ||
+      q_scale == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "phase2_tables: NULL argument");
+  if (B < 1 || n_alloc < 1 || n_layers < 1 || n_heads < 1)
+    return fail(TG_ERR_INVALID_ARGUMENT, "phase2_tables: B=%d n_alloc=%d n_layers=%d n_heads=%d", B,
+                n_alloc, n_layers, n_heads);
+  if ((int64_t)n_layers * n_heads > tg::kTablesMaxLH)
+    return fail(TG_ERR_UNSUPPORTED, "phase2_tables: n_layers * n_heads = %lld exceeds %d",
+                (long long)n_layers * n_heads, tg::kTablesMaxLH);
+  if (!(eps >= 0.f)) return fail(TG_ERR_INVALID_ARGUMENT, "phase2_tables: eps must be >= 0");
+  for (int b = 0; b < B; ++b) {
+    if (n_state[b] < 1 || state_begin[b] < 0)
+      return fail(TG_ERR_INVALID_ARGUMENT, "phase2_tables: request %d: state [%d, +%d)", b,
+                  state_begin[b], n_state[b]);
+    if (n_kept[b] < 1 || n_kept[b] > n_alloc)
+      return fail(TG_ERR_INVALID_ARGUMENT, "phase2_tables: request %d: n_kept %d outside [1, %d]", b,
+                  n_kept[b], n_alloc);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int b0 = 0; b0 < B; b0 += tg::kTablesMaxReq) {
+    const int nb = B - b0 < tg::kTablesMaxReq ? B - b0 : tg::kTablesMaxReq;
+    tg::TablesParams p;
+    memset(&p, 0, sizeof(p));
+    p.scores = scores + (int64_t)b0 * s_sb;
+    p.s_sb = s_sb;
+    p.keep = keep + (int64_t)b0 * keep_sb;
+    p.keep_sb = keep_sb;
+    p.gate_scale = gate_scale;
+    p.attn_scale = attn_scale;
+    // the tables keep the full batch's layout; this launch writes its requests
+    p.bias = bias + (int64_t)b0 * n_heads * n_alloc;
+    p.q_scale = q_scale + (int64_t)b0 * n_heads * n_alloc;
+    p.B = B;  // plane stride of the output
+    p.L = n_layers;
+    p.H = n_heads;
+    p.n_alloc = n_alloc;
+    p.eps = eps;
+    p.gain = gain;
+    for (int i = 0; i < nb; ++i) {
+      p.n_state[i] = n_state[b0 + i];
+      p.begin[i] = state_begin[b0 + i];
+      p.n_kept[i] = n_kept[b0 + i];
+    }
+    dim3 grid((unsigned)((n_alloc + tg::kTablesThreads - 1) / tg::kTablesThreads), (unsigned)nb);
+    tg::phase2_tables_kernel<<<grid, tg::kTablesThreads, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "phase2_tables launch");
+  }
   return TG_OK;
 }
 

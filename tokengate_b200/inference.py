@@ -21,7 +21,7 @@ from typing import List, Optional, Sequence, Union
 
 import torch
 
-from .gate import LinLogSigGate
+from .gate import SYNTHETIC_E2E_SEED, LinLogSigGate, load_gate, synthetic_e2e_gate
 from .model import patch_model, set_attention_backends_for_layers
 from .prefill import prefill_batch_for_decode
 
@@ -146,30 +146,36 @@ def synthetic_qwen3(name_or_dict, seed: int = 0, device="cuda", dtype=torch.bflo
 
 def load_model(checkpoint: Optional[str] = None, base_model=None, gate_layer: Optional[int] = None,
                gate_attn: str = "b200", dtype=None, *, model: Optional[torch.nn.Module] = None,
-               gate: Optional[torch.nn.Module] = None, device="cuda", seed: int = 0) -> TokenGateModel:
-    """Build a TokenGateModel on the B200 kernels.
+               gate=None, device="cuda", seed: int = 0, trusted_checkpoint: bool = False) -> TokenGateModel:
+    """Build a TokenGateModel on the B200 kernels (reference: tokengate/inference.py:141-180).
 
-    checkpoint : gate .pt ({"state_dict", "metadata"}) of a linear log-sigmoid
-        gate, or None when `gate` is passed (or for a random gate from `seed`).
+    checkpoint : a gate .pt. A finalized-gate checkpoint (the reference's
+        save_gate format: state_dict with gate_branch.* weights and the
+        finalized flags) is loaded with gate.load_gate; a linear log-sigmoid
+        gate checkpoint ({"state_dict": {"readout.weight"}, "metadata"}) is
+        loaded into LinLogSigGate. None when `gate` is passed (or for a
+        random gate from `seed`). Read with torch's weights-only unpickler
+        unless trusted_checkpoint.
     base_model : a QWEN3_SHAPES name / Qwen3Config kwargs (random init from
         `seed`), or a HF model id / path loadable by AutoModelForCausalLM;
         ignored when `model` is passed. Read from the checkpoint metadata when
         omitted, as in the reference.
     gate_layer : the gate's layer (metadata when omitted).
     gate_attn  : "b200" (or the reference's default name "fa2", same kernel).
+    gate       : a gate module, or "e2e" for a synthetic finalized gate
+                 (gate.synthetic_e2e_gate, seeded) on the model.
     """
     if dtype is None:
         dtype = torch.bfloat16
     if dtype != torch.bfloat16:
         raise NotImplementedError("the B200 kernels compute in bf16")
     meta = {}
-    state = None
+    blob = None
     if checkpoint is not None:
         if not os.path.isfile(checkpoint):
             raise FileNotFoundError(f"gate checkpoint not found: {checkpoint}")
-        blob = torch.load(checkpoint, map_location="cpu", weights_only=False)
-        meta = blob.get("metadata", {})
-        state = blob.get("state_dict", blob)
+        blob = torch.load(checkpoint, map_location="cpu", weights_only=not trusted_checkpoint)
+        meta = blob.get("metadata", {}) if isinstance(blob, dict) else {}
     if base_model is None:
         base_model = meta.get("base_model")
     if gate_layer is None:
@@ -185,10 +191,20 @@ def load_model(checkpoint: Optional[str] = None, base_model=None, gate_layer: Op
             from transformers import AutoModelForCausalLM
             model = AutoModelForCausalLM.from_pretrained(base_model, dtype=dtype).to(device).eval()
     hidden = model.config.hidden_size
+    dev = next(model.parameters()).device
+    if isinstance(gate, str):
+        if gate != "e2e":
+            raise ValueError(f"gate={gate!r}: pass a module or 'e2e'")
+        gate = synthetic_e2e_gate(model, int(gate_layer), seed=SYNTHETIC_E2E_SEED + seed, device=dev)
     if gate is None:
-        gate = LinLogSigGate(hidden, generator=torch.Generator().manual_seed(seed + 1))
-        if state is not None:
-            gate.load_state_dict(state)
+        state = blob.get("state_dict", blob) if isinstance(blob, dict) else None
+        if state is not None and any(k.startswith("gate_branch.") for k in state):
+            gate, _ = load_gate(blob)
+            gate = gate.to(dev).float().eval()
+        else:
+            gate = LinLogSigGate(hidden, generator=torch.Generator().manual_seed(seed + 1))
+            if state is not None:
+                gate.load_state_dict(state)
     patch_model(model)
     set_attention_backends_for_layers(model, gate_attn)
     name = base_model if isinstance(base_model, str) else "custom"

@@ -86,13 +86,16 @@ def fused_weights(model):
     return fw
 
 
-def layer_forward(lw: FusedLayerWeights, h: torch.Tensor, delta: Optional[torch.Tensor],
-                  cos: torch.Tensor, sin: torch.Tensor, cache, layer_idx: int,
-                  gate_bias: Optional[torch.Tensor] = None,
-                  q_row_scale: Optional[torch.Tensor] = None):
-    """One decoder layer. h: (B, S, H) residual stream (updated in place when
-    delta is given); delta: the previous layer's MLP output or None. Returns
-    (h, delta') with delta' this layer's MLP output, not yet added."""
+def layer_attention(lw: FusedLayerWeights, h: torch.Tensor, delta: Optional[torch.Tensor],
+                    cos: torch.Tensor, sin: torch.Tensor, cache, layer_idx: int,
+                    gate_bias: Optional[torch.Tensor] = None,
+                    q_row_scale: Optional[torch.Tensor] = None):
+    """The attention half of a decoder layer, up to the token-mixer residual.
+
+    h: (B, S, H) residual stream (updated in place when delta is given);
+    delta: the previous layer's MLP output or None. Returns (a, x2): a = the
+    residual after attention (the reference's a_j boundary of the split gate
+    layer, gate_forward.py:398-418) and x2 = post_attention_layernorm(a)."""
     B, S, H = h.shape
     h, x = ops.add_rmsnorm(h, delta, lw.in_w, lw.eps, h_out=h if delta is not None else None)
     q = F.linear(x, lw.wq).view(B, S, lw.n_q, lw.head_dim)
@@ -104,6 +107,21 @@ def layer_forward(lw: FusedLayerWeights, h: torch.Tensor, delta: Optional[torch.
         k, v = cache.update_tok(k, v, layer_idx)
     a = ops.keybias_attention(q, k, v, bias=gate_bias, causal=True, q_row_scale=q_row_scale)
     o = F.linear(a.view(B, S, -1), lw.wo)
-    h, x2 = ops.add_rmsnorm(h, o, lw.post_w, lw.eps, h_out=h)
-    act = ops.silu_mul(F.linear(x2, lw.wgu))
-    return h, F.linear(act, lw.wdown)
+    return ops.add_rmsnorm(h, o, lw.post_w, lw.eps, h_out=h)
+
+
+def layer_mlp(lw: FusedLayerWeights, x2: torch.Tensor) -> torch.Tensor:
+    """The MLP half on post_attention_layernorm output x2: returns the MLP output
+    (not yet added to the residual)."""
+    return F.linear(ops.silu_mul(F.linear(x2, lw.wgu)), lw.wdown)
+
+
+def layer_forward(lw: FusedLayerWeights, h: torch.Tensor, delta: Optional[torch.Tensor],
+                  cos: torch.Tensor, sin: torch.Tensor, cache, layer_idx: int,
+                  gate_bias: Optional[torch.Tensor] = None,
+                  q_row_scale: Optional[torch.Tensor] = None):
+    """One decoder layer. h: (B, S, H) residual stream (updated in place when
+    delta is given); delta: the previous layer's MLP output or None. Returns
+    (h, delta') with delta' this layer's MLP output, not yet added."""
+    h, x2 = layer_attention(lw, h, delta, cos, sin, cache, layer_idx, gate_bias, q_row_scale)
+    return h, layer_mlp(lw, x2)

@@ -381,3 +381,89 @@ def silu_mul(gu: torch.Tensor) -> torch.Tensor:
 def device_error(clear: bool = False) -> int:
     """Flags recorded by kernels whose bounded waits gave up on the current device (synchronises)."""
     return _lib.device_error(torch.cuda.current_stream().cuda_stream, clear)
+
+
+# ----------------------------------------------------------------- finalized gate
+def branch_score(gu: torch.Tensor, w_row: torch.Tensor, row_begin: Sequence[int],
+                 row_count: Sequence[int], out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Readout of the finalized gate's scoring branch over the fused [gate | up] rows.
+
+    scores[b, r] = bf16(sum_k bf16(bf16(silu(g_k)) * u_k) * w_row[k]) (as fp32, -0 -> +0)
+    with [g | u] = gu[b, row_begin[b] + r, :2*inter], for r < row_count[b].
+    gu: (B, S, >= 2*inter) bf16 with a contiguous last dim; w_row: (inter,) bf16.
+    Returns fp32 (B, max(row_count)); entries past row_count[b] untouched
+    (zero when allocated here).
+    """
+    _require_cuda("gu", gu, torch.bfloat16)
+    _require_cuda("w_row", w_row, torch.bfloat16)
+    if gu.dim() != 3 or gu.stride(-1) != 1:
+        raise ValueError("gu must be (B, S, 2*inter) with a contiguous last dim")
+    if w_row.dim() != 1 or not w_row.is_contiguous():
+        raise ValueError("w_row must be a contiguous vector")
+    B, S, W = gu.shape
+    inter = w_row.shape[0]
+    if W < 2 * inter:
+        raise ValueError(f"gu rows hold {W} values, need [gate | up] = {2 * inter}")
+    if len(row_begin) != B or len(row_count) != B:
+        raise ValueError("row_begin / row_count need one entry per request")
+    for b in range(B):
+        if row_begin[b] < 0 or row_count[b] < 0 or row_begin[b] + row_count[b] > S:
+            raise ValueError(f"request {b}: rows [{row_begin[b]}, {row_begin[b] + row_count[b]}) "
+                             f"outside [0, {S})")
+    n_max = max(int(c) for c in row_count)
+    if out is None:
+        out = torch.zeros((B, max(n_max, 1)), dtype=torch.float32, device=gu.device)
+    else:
+        _require_cuda("out", out, torch.float32)
+        if out.dim() != 2 or out.shape[0] != B or out.shape[1] < n_max or out.stride(1) != 1:
+            raise ValueError("out must be (B, >= max(row_count)) fp32 with a contiguous last dim")
+    L = _lib.lib()
+    with _device_ctx(gu):
+        _lib.check(L.tg_branch_score(gu.data_ptr(), gu.stride(0), gu.stride(1), inter, w_row.data_ptr(),
+                                     B, _i32_array(row_begin), _i32_array(row_count), out.data_ptr(),
+                                     out.stride(0), _stream(gu)))
+    return out
+
+
+def phase2_tables(scores: torch.Tensor, state_begin: Sequence[int], n_state: Sequence[int],
+                  keep: torch.Tensor, n_kept: Sequence[int], gate_scale: torch.Tensor,
+                  attn_scale: torch.Tensor, eps: float, gain: float = 1.0):
+    """Per-layer Phase-2 key bias and query scale of the finalized gate.
+
+    scores: raw branch scores fp32 (B, >= n_state[b]); keep: int64 (B, n_alloc)
+    kept positions; gate_scale / attn_scale: effective (softplus-applied)
+    (L', H) fp32. Returns (bias, q_scale), each fp32 (L', B, H, n_alloc):
+    layer l's slice is the (B, H, S) bias / q_row_scale of keybias_attention.
+    """
+    _require_cuda("scores", scores, torch.float32)
+    _require_cuda("keep", keep, torch.int64)
+    _require_cuda("gate_scale", gate_scale, torch.float32)
+    _require_cuda("attn_scale", attn_scale, torch.float32)
+    if scores.dim() != 2 or scores.stride(1) != 1:
+        raise ValueError("scores must be 2-D with a contiguous last dim")
+    if keep.dim() != 2 or keep.stride(1) != 1:
+        raise ValueError("keep must be 2-D with a contiguous last dim")
+    if gate_scale.dim() != 2 or gate_scale.shape != attn_scale.shape:
+        raise ValueError("gate_scale and attn_scale must both be (L', H)")
+    B, n_alloc = keep.shape
+    if scores.shape[0] != B:
+        raise ValueError("one score row per request")
+    for name, arr in (("state_begin", state_begin), ("n_state", n_state), ("n_kept", n_kept)):
+        if len(arr) != B:
+            raise ValueError(f"{name} needs one entry per request")
+    for b in range(B):
+        if n_state[b] > scores.shape[1]:
+            raise ValueError(f"request {b}: n_state {n_state[b]} exceeds the score row ({scores.shape[1]})")
+    Lp, H = gate_scale.shape
+    gs = gate_scale.contiguous()
+    at = attn_scale.contiguous()
+    bias = torch.empty((Lp, B, H, n_alloc), dtype=torch.float32, device=scores.device)
+    q_scale = torch.empty_like(bias)
+    L = _lib.lib()
+    with _device_ctx(scores):
+        _lib.check(L.tg_phase2_tables(scores.data_ptr(), scores.stride(0), B, _i32_array(state_begin),
+                                      _i32_array(n_state), keep.data_ptr(), keep.stride(0),
+                                      _i32_array(n_kept), int(n_alloc), gs.data_ptr(), at.data_ptr(),
+                                      int(Lp), int(H), float(eps), float(gain), bias.data_ptr(),
+                                      q_scale.data_ptr(), _stream(scores)))
+    return bias, q_scale

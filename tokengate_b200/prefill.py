@@ -18,6 +18,16 @@ Same control flow and return contract as the reference
             ORIGINAL positions;
   head      final norm of each request's last kept row -> lm_head -> argmax.
 
+With the finalized gate (E2EGate, a scoring branch attached) the gate layer
+is split at its attention residual a_j (split_gate_layer_mlp, :345-357):
+Phase 1 ends with layer L's attention half; the branch (LN2 -> fused
+[gate | up] GEMM -> branch_score readout) scores each request's state rows;
+selection is top-K of the raw score, which orders exactly like the
+reference's aggregate (a positive scaling of it; ties in one are ties in the
+other); phase2_tables builds every Phase-2 layer's per-head bias and
+scaled-softmax query scale in one launch; the gate layer's MLP runs on the
+kept rows at Phase-2 entry (gate_layer_mlp, :420-435).
+
 The reference's per-request Python loop for scoring/selection/gather and its
 host-side index construction are replaced by three batched launches; no host
 synchronisation happens between Phase 1 and the head.
@@ -28,8 +38,8 @@ from typing import List, Optional, Sequence, Union
 import torch
 
 from . import ops
-from .gate import readout_vector
-from .layers import fused_weights, layer_forward
+from .gate import e2e_kernel_weights, is_e2e_gate, readout_vector
+from .layers import fused_weights, layer_attention, layer_forward, layer_mlp
 from .model import PrefillCache, set_attn_scale_for_layers, set_gate_bias_for_layers
 
 # Phase-2 length bucket (the reference's set_phase2_bucket, gate_forward.py:531-546):
@@ -40,6 +50,27 @@ _PHASE2_BUCKET: Optional[int] = None
 def set_phase2_bucket(n: Optional[int]) -> None:
     global _PHASE2_BUCKET
     _PHASE2_BUCKET = None if n is None else int(n)
+
+
+# rows per scoring-branch GEMM: bounds the [gate | up] workspace (rows x 2*inter bf16)
+_BRANCH_CHUNK = 32768
+
+
+def _branch_scores(ew, x2: torch.Tensor, starts: Sequence[int], n_state: Sequence[int]) -> torch.Tensor:
+    """Raw scores of the finalized gate's branch over each request's state rows.
+
+    x2: (B, S, H) bf16 = post_attention_layernorm(a_j) of the gate layer. Each
+    request's state rows are contiguous, so the fused [gate | up] GEMM runs on
+    them directly (no gather), in chunks of _BRANCH_CHUNK rows, followed by the
+    branch_score readout. Returns fp32 (B, max n_state)."""
+    B = x2.shape[0]
+    scores = torch.empty((B, max(n_state)), dtype=torch.float32, device=x2.device)
+    for b in range(B):
+        for c0 in range(0, n_state[b], _BRANCH_CHUNK):
+            c1 = min(n_state[b], c0 + _BRANCH_CHUNK)
+            gu = torch.nn.functional.linear(x2[b, starts[b] + c0:starts[b] + c1], ew.wgu)
+            ops.branch_score(gu.unsqueeze(0), ew.w_row, [0], [c1 - c0], out=scores[b:b + 1, c0:])
+    return scores
 
 
 def _ids_to_device(prompt_ids_list, device) -> torch.Tensor:
@@ -89,10 +120,25 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
         if not 0 <= starts[b] < ends[b] <= lens[b]:
             raise ValueError(f"request {b}: state span [{starts[b]}, {ends[b]}) invalid for length {lens[b]}")
     max_seq_len = max(lens)
+    e2e = is_e2e_gate(gate)
     has_attn_scale = hasattr(gate, "attn_scale_eff") and not getattr(gate, "_baseline_no_bias_scale", False)
     if fused is None:
-        fused = not has_attn_scale
-    if fused and has_attn_scale:
+        fused = e2e or not has_attn_scale
+    if e2e:
+        if not fused:
+            raise NotImplementedError("the finalized gate is served by the fused layer path (fused=True)")
+        if getattr(gate, "selection_mode", "topk") != "topk" or getattr(gate, "random_topk", False):
+            raise NotImplementedError("only top-K selection is served by the B200 selection kernel")
+        if getattr(gate, "_baseline_no_bias_scale", False):
+            raise NotImplementedError("the selection-only baseline mode of the finalized gate is not served")
+        if gate.n_layers_bias != n_layers - 1 - gate_layer:
+            raise ValueError(f"n_layers_bias mismatch: gate has {gate.n_layers_bias} layer slots, the model "
+                             f"has {n_layers - 1 - gate_layer} layers above gate_layer={gate_layer}")
+        if gate.n_heads != model.config.num_attention_heads:
+            raise ValueError(f"gate has {gate.n_heads} heads, the model {model.config.num_attention_heads} "
+                             f"query heads (the bias is per Phase-2 query head)")
+        ew = e2e_kernel_weights(gate, device)
+    elif fused and has_attn_scale:
         raise NotImplementedError("the fused layer path serves gates without a learned attention scale")
     fw = fused_weights(model) if fused else None
 
@@ -103,12 +149,16 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
     position_ids = torch.arange(max_seq_len, device=device).unsqueeze(0).expand(B, -1)
     pe = inner.rotary_emb(hidden, position_ids)
     cache = PrefillCache(n_layers)
+    x2 = None
     if fused:
         cos, sin = pe
         delta = None
-        for i in range(gate_layer + 1):
+        for i in range(gate_layer if e2e else gate_layer + 1):
             hidden, delta = layer_forward(fw[i], hidden, delta, cos, sin, cache, i)
-        hidden, _ = ops.add_rmsnorm(hidden, delta, None, 0.0, h_out=hidden, want_x=False)
+        if e2e:   # Phase 1 ends at the gate layer's attention residual a_j
+            hidden, x2 = layer_attention(fw[gate_layer], hidden, delta, cos, sin, cache, gate_layer)
+        else:
+            hidden, _ = ops.add_rmsnorm(hidden, delta, None, 0.0, h_out=hidden, want_x=False)
         del delta, cos, sin
     else:
         for i in range(gate_layer + 1):
@@ -117,16 +167,28 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
     del pe
 
     # ---- score + select
-    w = readout_vector(gate, hidden.shape[-1], device)
     n_state = [e - s for s, e in zip(starts, ends)]
-    scores = ops.gate_score(hidden, w, starts, n_state)
+    if e2e:
+        scores = _branch_scores(ew, x2, starts, n_state)
+        del x2
+    else:
+        w = readout_vector(gate, hidden.shape[-1], device)
+        scores = ops.gate_score(hidden, w, starts, n_state)
     Ks = list(K) if isinstance(K, (list, tuple)) else [K] * B
     K_clampeds = [max(1, min(int(Ks[b]), n_state[b])) for b in range(B)]
     n_kepts = [starts[b] + K_clampeds[b] + (lens[b] - ends[b]) for b in range(B)]
     max_n_kept = max(n_kepts)
     n_alloc = max_n_kept if _PHASE2_BUCKET is None else -(-max_n_kept // _PHASE2_BUCKET) * _PHASE2_BUCKET
-    kept_positions, bias_row, _ = ops.topk_select(scores, n_state, K_clampeds, starts, lens,
-                                                  n_alloc, bias_dtype=hidden.dtype)
+    if e2e:
+        # every aggregate 0 when all first-layer scales are 0: index order decides
+        sel = torch.zeros_like(scores) if ew.degenerate else scores
+        kept_positions, bias_row, _ = ops.topk_select(sel, n_state, K_clampeds, starts, lens, n_alloc,
+                                                      bias_dtype=None)
+        bias_tab, qs_tab = ops.phase2_tables(scores, starts, n_state, kept_positions, n_kepts,
+                                             ew.gate_scale, ew.attn_scale, ew.eps, ew.gain)
+    else:
+        kept_positions, bias_row, _ = ops.topk_select(scores, n_state, K_clampeds, starts, lens,
+                                                      n_alloc, bias_dtype=hidden.dtype)
 
     # ---- compact
     H = hidden.shape[-1]
@@ -153,14 +215,26 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
     del hidden, scores
 
     # ---- Phase 2
-    # The reference hands the bf16 bias to every layer and each converts it to
-    # fp32 (_bias_bhs); converting once here gives the same values.
-    gate_bias = bias_row.float()
     pe2 = inner.rotary_emb(hs_pruned, kept_positions)
     last_valid = torch.tensor([n - 1 for n in n_kepts], device=device)
     rows = torch.arange(B, device=device)
-    if fused:
-        bias3 = gate_bias.unsqueeze(1)                      # (B, 1, n_alloc): one row for all heads
+    if e2e:
+        cos2, sin2 = pe2
+        # Phase-2 entry: the gate layer's own MLP on the kept rows (zero pad rows stay zero)
+        _, x2p = ops.add_rmsnorm(hs_pruned, None, fw[gate_layer].post_w, fw[gate_layer].eps)
+        delta = layer_mlp(fw[gate_layer], x2p)
+        del x2p
+        for i in range(gate_layer + 1, n_layers):
+            li = i - gate_layer - 1
+            hs_pruned, delta = layer_forward(fw[i], hs_pruned, delta, cos2, sin2, cache, i,
+                                             gate_bias=bias_tab[li], q_row_scale=qs_tab[li])
+        h_last = hs_pruned[rows, last_valid]
+        _, hs_last = ops.add_rmsnorm(h_last, delta[rows, last_valid], inner.norm.weight,
+                                     float(inner.norm.variance_epsilon))
+    elif fused:
+        # The reference hands the bf16 bias to every layer and each converts it to
+        # fp32 (_bias_bhs); converting once here gives the same values.
+        bias3 = bias_row.float().unsqueeze(1)               # (B, 1, n_alloc): one row for all heads
         cos2, sin2 = pe2
         delta = None
         for i in range(gate_layer + 1, n_layers):
@@ -171,6 +245,7 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
         _, hs_last = ops.add_rmsnorm(h_last, delta[rows, last_valid], inner.norm.weight,
                                      float(inner.norm.variance_epsilon))
     else:
+        gate_bias = bias_row.float()
         set_gate_bias_for_layers(model, gate_layer + 1, n_layers, gate_bias, per_head=False)
         attn_scale = gate.attn_scale_eff() if has_attn_scale else None
         set_attn_scale_for_layers(model, gate_layer + 1, n_layers, attn_scale)
