@@ -171,3 +171,22 @@ def test_synthetic_gate_and_oracle_prefill_vs_reference():
         assert out["kept_positions"][b] == d["kept"][b, :d["n_kepts"][b]].tolist()
     assert out["first_tokens"].tolist() == d["first_tokens"].tolist()
     assert np.abs(out["logits"].numpy() - d["logits"]).max() <= 1e-4
+
+
+def test_module_path_phase2_prologue_vs_reference(fx):
+    """The patched attention module's Phase-2 prologue (used when the transformers
+    layers run the B200 attention) forms s_eff and the scaled bias exactly as the
+    reference's _phase2_q_bias does (bf16, bit for bit)."""
+    from types import SimpleNamespace
+    from tokengate_b200.model import _phase2_q_scale_and_bias
+    z, gate, _ = fx
+    eff = gate.attn_scale_eff().detach()
+    r = torch.from_numpy(z["ssmax_ratio"])
+    gb = torch.from_numpy(z["gate_bias_batched"].view(np.int16)).view(torch.bfloat16)
+    B, n = r.shape
+    for l in range(gate.n_layers_bias):
+        mod = SimpleNamespace(attn_scale=eff[l], ssmax_ratio=r, gate_bias=gb[..., l, :], _gate_per_head=True)
+        qs, bias = _phase2_q_scale_and_bias(mod, B, n, torch.bfloat16)
+        assert np.array_equal(qs.numpy(), ge.bf16_bits_to_f32(z[f"L{l}_s_eff"]))
+        assert bias.dtype == torch.bfloat16
+        assert np.array_equal(bias.view(torch.int16).numpy().view(np.uint16), z[f"L{l}_bias"])

@@ -34,9 +34,10 @@
 //                             = the reference's q * s_eff in bf16)
 //   Output layout (L', B, H, n_alloc) fp32 for both tables: layer l's slice is
 //   the (B, H, S) bias / q-row-scale operand of the key-bias attention.
-//   The variance reduction runs in a fixed order (thread-strided partials over
-//   256 threads, xor butterfly, warps in order) and is repeated identically by
-//   every CTA of a request.
+//   The variance reduction runs in a fixed order (four partial sums per thread
+//   over 16-byte vectors, xor butterfly, warps in order) and is repeated
+//   identically by every CTA of a request; CTAs split the slots, the requests
+//   and groups of layers so that a few hundred CTAs share the writes.
 #pragma once
 
 #include "ptx.cuh"
@@ -171,12 +172,16 @@ struct TablesParams {
   float* bias;              // (L', B, H, n_alloc)
   float* q_scale;           // (L', B, H, n_alloc)
   int B, L, H, n_alloc;
+  int layers_per_cta;
   float eps, gain;
   int n_state[kTablesMaxReq];
   int begin[kTablesMaxReq];
   int n_kept[kTablesMaxReq];
 };
 
+// grid (slot chunks of kTablesThreads, requests, layer groups): blockIdx.z
+// covers layers [z * layers_per_cta, ...). Every CTA of a request computes the
+// same rs (same loads, same order); the scores row is read from L2.
 __global__ void __launch_bounds__(kTablesThreads) phase2_tables_kernel(const TablesParams p) {
   __shared__ float s_g[kTablesMaxLH];
   __shared__ float s_s[kTablesMaxLH];  // bf16(S_eff) as fp32
@@ -184,19 +189,32 @@ __global__ void __launch_bounds__(kTablesThreads) phase2_tables_kernel(const Tab
   __shared__ float s_rs;
   const int b = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int LH = p.L * p.H;
-  for (int i = threadIdx.x; i < LH; i += kTablesThreads) {
-    s_g[i] = p.gate_scale[i];
-    s_s[i] = bf16_round(p.attn_scale[i]);
+  const int l0 = blockIdx.z * p.layers_per_cta;
+  const int l1 = min(p.L, l0 + p.layers_per_cta);
+  for (int i = threadIdx.x; i < (l1 - l0) * p.H; i += kTablesThreads) {
+    s_g[i] = p.gate_scale[l0 * p.H + i];
+    s_s[i] = bf16_round(p.attn_scale[l0 * p.H + i]);
   }
-  // ---- rs of request b (same order in every CTA of the request)
+  // ---- rs of request b: four independent partial sums per thread over
+  // 16-byte vectors (scalar head / tail), combined in a fixed order
   const float* x = p.scores + (int64_t)b * p.s_sb;
   const int n = p.n_state[b];
-  float acc = 0.f;
-  for (int i = threadIdx.x; i < n; i += kTablesThreads) {
-    const float v = x[i];
-    acc = __fmaf_rn(v, v, acc);
+  const int head = (int)(((16 - (reinterpret_cast<uintptr_t>(x) & 15)) & 15) >> 2);
+  const int lead = head < n ? head : n;
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  if ((int)threadIdx.x < lead) a0 = __fmul_rn(x[threadIdx.x], x[threadIdx.x]);
+  const float4* xv = reinterpret_cast<const float4*>(x + lead);
+  const int nv = (n - lead) >> 2;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < nv; i += kTablesThreads) {
+    const float4 v = __ldg(xv + i);
+    a0 = __fmaf_rn(v.x, v.x, a0);
+    a1 = __fmaf_rn(v.y, v.y, a1);
+    a2 = __fmaf_rn(v.z, v.z, a2);
+    a3 = __fmaf_rn(v.w, v.w, a3);
   }
+  for (int i = lead + 4 * nv + threadIdx.x; i < n; i += kTablesThreads) a1 = __fmaf_rn(x[i], x[i], a1);
+  float acc = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
   if (lane == 0) s_warp[warp] = acc;
@@ -224,18 +242,20 @@ __global__ void __launch_bounds__(kTablesThreads) phase2_tables_kernel(const Tab
   const float inv_h = __frcp_rn((float)p.H);
   const float pad_b = bf16_round(-1e9f);
   const int64_t plane = (int64_t)p.B * p.H * p.n_alloc;
-  for (int l = 0; l < p.L; ++l) {
+  for (int l = l0; l < l1; ++l) {
+    const float* gl = s_g + (l - l0) * p.H;
+    const float* sl = s_s + (l - l0) * p.H;
     float sum = 0.f;
     float* qrow = p.q_scale + l * plane + ((int64_t)b * p.H) * p.n_alloc + t;
     for (int h = 0; h < p.H; ++h) {
-      const float se = bf16_round(__fmul_rn(s_s[l * p.H + h], r));
+      const float se = bf16_round(__fmul_rn(sl[h], r));
       qrow[(int64_t)h * p.n_alloc] = se;
       sum = __fadd_rn(sum, se);
     }
     const float sb = bf16_round(__fmul_rn(sum, inv_h));
     float* brow = p.bias + l * plane + ((int64_t)b * p.H) * p.n_alloc + t;
     for (int h = 0; h < p.H; ++h) {
-      const float base = kind == 0 ? bf16_round(__fmul_rn(bn, s_g[l * p.H + h])) : (kind == 2 ? pad_b : 0.0f);
+      const float base = kind == 0 ? bf16_round(__fmul_rn(bn, gl[h])) : (kind == 2 ? pad_b : 0.0f);
       brow[(int64_t)h * p.n_alloc] = bf16_round(__fmul_rn(base, sb));
     }
   }

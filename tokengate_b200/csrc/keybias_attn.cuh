@@ -57,6 +57,15 @@ constexpr int kSmKExt = kSmV + 2 * kAttnTileBytes;       // 2 stages: K bias ext
 constexpr int kSmQExt = kSmKExt + 2 * kExtBytes;         // 2 tiles: Q one-hot extension
 constexpr int kSmBar = kSmQExt + 2 * kExtBytes;
 constexpr int kNumBars = 17;
+
+// pairs q (0..31 per 64-key half) with (q & kAttnPolyMask) == kAttnPolyMask take
+// exp2 on the FMA pipe (degree-3 polynomial) instead of the MUFU; a mask of
+// -1 keeps every exp2 on the MUFU
+#ifndef TG_ATTN_POLY_MASK
+#define TG_ATTN_POLY_MASK -1
+#endif
+constexpr int kAttnPolyMask = TG_ATTN_POLY_MASK;
+
 constexpr int kSmTmemSlot = kSmBar + kNumBars * 8;
 constexpr int kAttnSmemBytes = kSmTmemSlot + 16 + 1024;  // + alignment slack
 
@@ -68,10 +77,10 @@ enum {
   BAR_V_FULL = 5,   // 2
   BAR_V_EMPTY = 7,  // 2
   BAR_S_FULL = 9,   // 2 (per tile)
-  BAR_P_FULL = 11,  // 2 (per tile)
-  BAR_O_FULL = 13,  // 2 (per tile)
-  BAR_MMA_DONE = 15,
-  BAR_Q_READY = 16  // softmax warps scaled their Q rows (only with a row scale)
+  BAR_O_FULL = 11,  // 2 (per tile)
+  BAR_MMA_DONE = 13,
+  BAR_Q_READY = 14, // softmax warps scaled their Q rows (only with a row scale)
+  BAR_P_FULL = 15   // 2 (per tile)
 };
 
 // device error bits
@@ -172,6 +181,7 @@ __device__ __forceinline__ uint32_t split_bf16x2(float v) {
   return (uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(lo) << 16);
 }
 
+template <bool kHasBias>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     keybias_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k,
@@ -189,7 +199,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.y;
-  const bool has_bias = p.bias != nullptr;
+  constexpr bool has_bias = kHasBias;
   const bool has_qscale = p.qscale != nullptr;
 
   TileInfo ti[2];
@@ -238,11 +248,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   // Register split (launch: 384 threads x 168 = 64512): the two softmax
-  // warpgroups take 224 each, the producer/MMA warpgroup keeps 56:
-  // 2*128*224 + 128*56 = 64512. Each role's code is dominated by its own
-  // setmaxnreg so the allocator gives it that budget.
+  // warpgroups take 216 each, the producer/MMA warpgroup keeps 72:
+  // 2*128*216 + 128*72 = 64512 (no spills in either role). Each role's code
+  // is dominated by its own setmaxnreg so the allocator gives it that budget.
   if (warp >= kProducerWarp) {
-  setmaxnreg_dec<56>();
+  setmaxnreg_dec<72>();
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -321,6 +331,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
+    // One thread issues every MMA; a tcgen05.mma occupies the issuing thread
+    // for about the time the tensor pipe needs for one 128x128x16 step, so
+    // the steady-state loop below carries nothing but the MMAs, the waits
+    // they depend on (one try_wait each when already complete) and the
+    // commits the other roles wait for.
     if (lane == 0) {
       constexpr uint32_t kIdescQK = umma_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t kIdescPV = umma_idesc_bf16(128, 128, 0, 1);
@@ -332,7 +347,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           umma_ss(tmem + t * 128u, umma_desc_sw128(qa + off, 16, 1024),
                   umma_desc_sw128(ka + off, 16, 1024), kIdescQK, kk > 0);
         }
-        if (has_bias)
+        if constexpr (kHasBias)
           umma_ss(tmem + t * 128u, umma_desc_sw32(sQExt + t * kExtBytes, 16, 256),
                   umma_desc_sw32(sKExt + s * kExtBytes, 16, 256), kIdescQK, 1u);
       };
@@ -349,7 +364,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (ok && has_qscale) ok = mbar_wait(bar(BAR_Q_READY), 0, p.err, ERR_ATTN_Q_READY);
       if (ok && nblk > 0) ok = mbar_wait(bar(BAR_K_FULL + 0), 0, p.err, ERR_ATTN_K_FULL);
       if (ok && nblk > 0) {
-        tc_fence_after();
         for (int t = 0; t < 2; ++t) {
           if (ti[t].nblk > 0) {
             issue_qk(t, 0);
@@ -358,9 +372,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         umma_commit(bar(BAR_K_EMPTY + 0));
       }
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int s = j & 1;
-        const int s1 = (j + 1) & 1;
+      // steady state: both tiles need blocks j and j + 1
+      const int nboth = min(ti[0].nblk, ti[1].nblk) - 1;
+      int j = 0;
+      for (; ok && j < nboth; ++j) {
+        const int s = j & 1, s1 = s ^ 1;
+        const uint32_t ph = (j >> 1) & 1, ph1 = ((j + 1) >> 1) & 1, pp = j & 1;
+        if (!mbar_wait(bar(BAR_V_FULL + s), ph, p.err, ERR_ATTN_V_FULL)) { ok = false; break; }
+        if (!mbar_wait(bar(BAR_P_FULL + 0), pp, p.err, ERR_ATTN_P_FULL)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(0, s, j > 0);
+        if (!mbar_wait(bar(BAR_K_FULL + s1), ph1, p.err, ERR_ATTN_K_FULL)) { ok = false; break; }
+        issue_qk(0, s1);
+        umma_commit(bar(BAR_S_FULL + 0));
+        if (!mbar_wait(bar(BAR_P_FULL + 1), pp, p.err, ERR_ATTN_P_FULL)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(1, s, j > 0);
+        umma_commit(bar(BAR_V_EMPTY + s));
+        issue_qk(1, s1);
+        umma_commit(bar(BAR_S_FULL + 1));
+        umma_commit(bar(BAR_K_EMPTY + s1));
+      }
+      // tail: the blocks where one tile has finished or no next block exists
+      for (; ok && j < nblk; ++j) {
+        const int s = j & 1, s1 = s ^ 1;
         const bool more = (j + 1) < nblk;
         if (!mbar_wait(bar(BAR_V_FULL + s), (j >> 1) & 1, p.err, ERR_ATTN_V_FULL)) break;
         if (j < ti[0].nblk) {
@@ -371,7 +406,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         if (more) {
           if (!mbar_wait(bar(BAR_K_FULL + s1), ((j + 1) >> 1) & 1, p.err, ERR_ATTN_K_FULL)) break;
-          tc_fence_after();
           if (j + 1 < ti[0].nblk) {
             issue_qk(0, s1);
             umma_commit(bar(BAR_S_FULL + 0));
@@ -399,7 +433,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncwarp();
   }
   } else {
-    setmaxnreg_inc<224>();
+    setmaxnreg_inc<216>();
     // ------------------------------------------------------------ softmax
     const int t = warp >> 2;
     const int sub = warp & 3;
@@ -463,15 +497,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int c = 0; c < 128; ++c)
           if (c > lim) sv[c] = __float_as_uint(-INFINITY);
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+      // row max: eight independent 3-input-max chains (the chains' latency,
+      // not the instruction count, bounds this step), then a short tree
+      float mxa[8];
 #pragma unroll
-      for (int c = 0; c < 128; c += 8) {
-        mx0 = fmax3(mx0, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
-        mx1 = fmax3(mx1, __uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]));
-        mx2 = fmax3(mx2, __uint_as_float(sv[c + 4]), __uint_as_float(sv[c + 5]));
-        mx3 = fmax3(mx3, __uint_as_float(sv[c + 6]), __uint_as_float(sv[c + 7]));
+      for (int a = 0; a < 8; ++a) mxa[a] = fmaxf(__uint_as_float(sv[2 * a]), __uint_as_float(sv[2 * a + 1]));
+#pragma unroll
+      for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+        for (int a = 0; a < 8; ++a)
+          mxa[a] = fmax3(mxa[a], __uint_as_float(sv[c + 2 * a]), __uint_as_float(sv[c + 2 * a + 1]));
       }
-      const float mx = fmax3(fmaxf(mx0, mx1), mx2, mx3) * c2;
+      const float mx = fmaxf(fmax3(mxa[0], mxa[1], mxa[2]), fmaxf(fmax3(mxa[3], mxa[4], mxa[5]),
+                                                                   fmaxf(mxa[6], mxa[7]))) * c2;
 
       // lazy max: move it (and rescale O) only when it grows by more than 8 in
       // log2 units; O is stable here because S_t(j) completing implies the
@@ -487,30 +525,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         l_run *= alpha;
         m_run = m_new;
       }
-      const float msub = (m_run == -INFINITY) ? 0.f : m_run;
-      const float2 negm = make_float2(-msub, -msub);
-
-      // p = 2^(S*c2 - m): one FFMA2 per pair, exp2 on the MUFU (measured
-      // faster here than moving a share of the pairs to an FMA-pipe
-      // polynomial); packed bf16 pairs written in two halves
-      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int c = half * 64 + 2 * q;
-          const float2 d = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
-                                      c22, negm);
-          float2 pp;
-          pp.x = ex2_approx(d.x);
-          pp.y = ex2_approx(d.y);
-          if (q & 1) ls1 = __fadd2_rn(ls1, pp); else ls0 = __fadd2_rn(ls0, pp);
-          pk[q] = pack_bf16x2(pp.x, pp.y);
-        }
-        tmem_st32(tS + half * 32, pk);
-      }
-      l_run += (ls0.x + ls0.y) + (ls1.x + ls1.y);
+      // O must be rescaled before this block's first P half is published
+      // (the P V MMA accumulates into it)
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -521,9 +537,40 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_st32(tO + c * 32, o);
         }
       }
+      const float msub = (m_run == -INFINITY) ? 0.f : m_run;
+      const float2 negm = make_float2(-msub, -msub);
+
+      // p = 2^(S*c2 - m): one FFMA2 per pair, exp2 on the MUFU except for the
+      // pairs the poly mask assigns to the FMA pipe; P is stored as packed
+      // bf16 pairs in two 64-key halves and published once both are in TMEM
+      float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                      make_float2(0.f, 0.f)};
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const int c = half * 64 + 2 * q;
+          const float2 d = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
+                                      c22, negm);
+          float2 pp;
+          if (kAttnPolyMask >= 0 && (q & kAttnPolyMask) == kAttnPolyMask) {
+            pp = exp2_poly2_lean(d);
+          } else {
+            pp.x = ex2_approx(d.x);
+            pp.y = ex2_approx(d.y);
+          }
+          ls[q & 3] = __fadd2_rn(ls[q & 3], pp);
+          pk[q] = pack_bf16x2(pp.x, pp.y);
+        }
+        tmem_st32_async(tS + half * 32, pk);
+      }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_P_FULL + t));
+      const float2 lsum = __fadd2_rn(__fadd2_rn(ls[0], ls[1]), __fadd2_rn(ls[2], ls[3]));
+      l_run += lsum.x + lsum.y;
     }
 
     if (ok && me.nblk > 0) {

@@ -56,9 +56,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 // Waits for the phase with the given parity to complete. Returns false (and
 // ORs `code` into *err) if it has not completed within kWaitTimeoutNs.
+// A phase that has already completed costs one try_wait; the polling loop
+// is the unlikely branch.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int* err,
                                           unsigned int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (__builtin_expect(mbar_try_wait(bar, parity), 1)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
@@ -227,6 +229,16 @@ __device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&r)[64
                :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32]), "r"(r[33]), "r"(r[34]), "r"(r[35]), "r"(r[36]), "r"(r[37]), "r"(r[38]), "r"(r[39]), "r"(r[40]), "r"(r[41]), "r"(r[42]), "r"(r[43]), "r"(r[44]), "r"(r[45]), "r"(r[46]), "r"(r[47]), "r"(r[48]), "r"(r[49]), "r"(r[50]), "r"(r[51]), "r"(r[52]), "r"(r[53]), "r"(r[54]), "r"(r[55]), "r"(r[56]), "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]), "r"(r[62]), "r"(r[63]) : "memory");
 }
 
+// tcgen05.st of 32 columns without the wait: pair with tmem_wait_st() before
+// the stored values are published to the tensor core.
+__device__ __forceinline__ void tmem_st32_async(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
+               :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+
 // 16-byte read-only global load that does not allocate in L1 (streamed data).
 __device__ __forceinline__ uint4 ld_nc_v4(const uint4* ptr) {
   uint4 v;
@@ -248,24 +260,24 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for two values on the FMA pipe: x clamped to [-120, 64], rounded to
-// n + f with |f| <= 1/2 by the 1.5*2^23 shifter, 2^f from a degree-3
-// polynomial fitted (relative minimax, 7.5e-5) on [-1/2, 1/2], and n added
-// to the exponent field. For inputs below -120 it returns 2^-120, not 0.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  x.x = fminf(fmaxf(x.x, -120.f), 64.f);
-  x.y = fminf(fmaxf(x.y, -120.f), 64.f);
+// 2^x for two values, x <= 64, on the FMA pipe: one lower clamp (at -126,
+// where 2^x is below every bf16 P that matters and the exponent field stays
+// in range), rounding to n + f with |f| <= 1/2 by the 1.5*2^23 shifter, 2^f
+// from a degree-3 polynomial fitted on [-1/2, 1/2] (relative minimax,
+// 7.5e-5), and n added to the exponent field with one shift-add per value.
+__device__ __forceinline__ float2 exp2_poly2_lean(float2 x) {
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
   const float2 shifter = make_float2(12582912.f, 12582912.f);
   const float2 t = __fadd2_rn(x, shifter);
-  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
-  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  const float2 f = __fadd2_rn(x, __fadd2_rn(shifter, make_float2(-t.x, -t.y)));
   float2 q = __ffma2_rn(make_float2(0.05517097935f, 0.05517097935f), f,
                         make_float2(0.24260970950f, 0.24260970950f));
   q = __ffma2_rn(q, f, make_float2(0.69326096773f, 0.69326096773f));
   q = __ffma2_rn(q, f, make_float2(0.99992817640f, 0.99992817640f));
   float2 r;
-  r.x = __int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23));
-  r.y = __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23));
+  r.x = __int_as_float((__float_as_int(t.x) << 23) + __float_as_int(q.x));
+  r.y = __int_as_float((__float_as_int(t.y) << 23) + __float_as_int(q.y));
   return r;
 }
 

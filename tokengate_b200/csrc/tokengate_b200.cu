@@ -219,16 +219,23 @@ int tg_keybias_attn_fwd(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_attn_attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(tg::keybias_attn_fwd_kernel,
+      cudaError_t e = cudaFuncSetAttribute(tg::keybias_attn_fwd_kernel<true>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            tg::kAttnSmemBytes);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tg::keybias_attn_fwd_kernel<false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kAttnSmemBytes);
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention smem)");
       g_attn_attr_set[dev] = true;
     }
   }
   dim3 grid((unsigned)units, (unsigned)B);
-  tg::keybias_attn_fwd_kernel<<<grid, tg::kAttnThreads, tg::kAttnSmemBytes,
-                                static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  if (p.bias != nullptr)
+    tg::keybias_attn_fwd_kernel<true><<<grid, tg::kAttnThreads, tg::kAttnSmemBytes,
+                                        static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  else
+    tg::keybias_attn_fwd_kernel<false><<<grid, tg::kAttnThreads, tg::kAttnSmemBytes,
+                                         static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "keybias attention launch");
   return TG_OK;
@@ -617,7 +624,15 @@ int tg_phase2_tables(const float* scores, int64_t s_sb, int B, const int32_t* st
       p.begin[i] = state_begin[b0 + i];
       p.n_kept[i] = n_kept[b0 + i];
     }
-    dim3 grid((unsigned)((n_alloc + tg::kTablesThreads - 1) / tg::kTablesThreads), (unsigned)nb);
+    // layer groups: about 3 CTAs per SM in total, at least one layer per CTA
+    const int64_t chunks = (n_alloc + tg::kTablesThreads - 1) / tg::kTablesThreads;
+    const int64_t target = 3LL * sm_count();
+    int64_t groups = (target + chunks * nb - 1) / (chunks * nb);
+    if (groups > n_layers) groups = n_layers;
+    if (groups < 1) groups = 1;
+    p.layers_per_cta = (int)((n_layers + groups - 1) / groups);
+    groups = (n_layers + p.layers_per_cta - 1) / p.layers_per_cta;
+    dim3 grid((unsigned)chunks, (unsigned)nb, (unsigned)groups);
     tg::phase2_tables_kernel<<<grid, tg::kTablesThreads, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "phase2_tables launch");

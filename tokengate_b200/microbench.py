@@ -4,11 +4,16 @@
     python -m tokengate_b200.microbench score  [--seq 32768] [--batch 1] [--iters 20]
     python -m tokengate_b200.microbench topk   [--k 2000] [--batch 1] [--iters 20]
     python -m tokengate_b200.microbench gather [--k 2000] [--batch 1] [--iters 20]
+    python -m tokengate_b200.microbench branch [--seq 32768] [--inter 6144] [--batch 1]
+    python -m tokengate_b200.microbench tables [--k 2000] [--layers 26] [--hq 16] [--batch 1]
 
 Prints one JSON line per run with the CUDA-event time per launch and the
 algorithmic FLOPs or bytes of one launch (attention: 4*B*Hq*D*S(S+1)/2;
 score: the bf16 state rows + w + fp32 scores; topk: scores read + keep/bias
-written; gather: hidden rows + 4 below-gate K/V tensors read and written).
+written; gather: hidden rows + 4 below-gate K/V tensors read and written;
+branch: the bf16 [gate | up] state rows + w + fp32 scores; tables: the raw
+scores and kept positions read once + both fp32 (L', B, H, n_alloc) tables
+written).
 """
 import argparse
 import json
@@ -33,7 +38,9 @@ def _time(fn, iters, warmup=3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=("attn", "score", "topk", "gather"))
+    ap.add_argument("kernel", choices=("attn", "score", "topk", "gather", "branch", "tables"))
+    ap.add_argument("--inter", type=int, default=6144)
+    ap.add_argument("--layers", type=int, default=26)
     ap.add_argument("--seq", type=int, default=32768)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--hq", type=int, default=16)
@@ -56,6 +63,27 @@ def main(argv=None):
         flops = 4.0 * B * a.hq * 128 * S * (S + 1) / 2
         res.update(seq=S, hq=a.hq, hkv=a.hkv, bias=not a.no_bias, ms=ms, tflop=flops / 1e12,
                    tflops=flops / ms / 1e9)
+    elif a.kernel == "branch":
+        n_art = S - 768
+        gu = torch.randn(B, n_art, 2 * a.inter, device=dev, dtype=torch.bfloat16, generator=g)
+        w = (torch.randn(a.inter, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        sc = ops.branch_score(gu, w, [0] * B, [n_art] * B)
+        ms = _time(lambda: ops.branch_score(gu, w, [0] * B, [n_art] * B, out=sc), a.iters)
+        byts = B * n_art * (4 * a.inter + 4) + 2 * a.inter
+        res.update(seq=S, inter=a.inter, ms=ms, us=ms * 1e3, mbytes=byts / 1e6, gbs=byts / ms / 1e6)
+    elif a.kernel == "tables":
+        st0, st1 = 512, S - 256
+        n_art = st1 - st0
+        sc = (torch.randn(B, n_art, device=dev, generator=g) * 0.5).to(torch.bfloat16).float()
+        n_kept = st0 + a.k + (S - st1)
+        keep, _, _ = ops.topk_select(sc, [n_art] * B, [a.k] * B, [st0] * B, [S] * B, n_kept, bias_dtype=None)
+        gs = torch.rand(a.layers, a.hq, device=dev, generator=g) + 0.5
+        at = torch.rand(a.layers, a.hq, device=dev, generator=g) + 0.5
+        fn = lambda: ops.phase2_tables(sc, [st0] * B, [n_art] * B, keep, [n_kept] * B, gs, at, 1e-6)
+        ms = _time(fn, a.iters)
+        byts = B * (n_art * 4 + n_kept * 8 + 2 * a.layers * a.hq * n_kept * 4)
+        res.update(seq=S, k=a.k, layers=a.layers, hq=a.hq, ms=ms, us=ms * 1e3, mbytes=byts / 1e6,
+                   gbs=byts / ms / 1e6)
     else:
         st0, st1 = 512, S - 256
         n_art = st1 - st0

@@ -89,34 +89,37 @@ def _rope_tok(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Te
 
 
 def _phase2_q_scale_and_bias(self, B: int, S: int, dtype):
-    """(q_row_scale (B|1, H|1, S) fp32 or None, extra softmax scale factor, bias) per
-    the reference's _phase2_q_bias (qwen3_flex_attention.py:447-473), with the query
-    scaling applied to the logits inside the kernel instead of to q."""
+    """(q_row_scale (B|1, H|1, S) fp32 or None, bias) per the reference's
+    _phase2_q_bias / _ssmax_s_eff (qwen3_flex_attention.py:417-473) at its
+    rounding points: the scales are formed in the query dtype (attn_scale and
+    the ssmax ratio cast to it, their product rounded to it), the kernel rounds
+    q * q_row_scale to bf16 exactly as the reference's q * s_eff is rounded,
+    and the bias is scaled in its own dtype."""
     per_head = getattr(self, "_gate_per_head", False)
     bias = self.gate_bias
     if self.attn_scale is not None and getattr(self, "ssmax_ratio", None) is not None:
-        gamma = self.attn_scale.float()
-        r = self.ssmax_ratio.float()
+        gamma = self.attn_scale.to(dtype)
+        r = self.ssmax_ratio.to(dtype)
         if r.dim() == 1:
             r = r.unsqueeze(0).expand(B, -1)
         g = gamma.view(1, -1, 1) if gamma.numel() > 1 else gamma.reshape(1, 1, 1)
-        s_eff = g * r.unsqueeze(1)                                    # (B, H|1, S)
+        s_eff = g * r.unsqueeze(1)                                    # (B, H|1, S) in dtype
         if bias is not None:
             sb = s_eff.mean(dim=1) if s_eff.shape[1] > 1 else s_eff[:, 0]   # (B, S)
             bias = bias * (sb.unsqueeze(-1) if bias.dim() == 3 else sb[0].unsqueeze(-1)
                            if bias.dim() == 2 else sb[0])
-        return s_eff.contiguous(), 1.0, bias
+        return s_eff.float().contiguous(), bias
     if self.attn_scale is not None:
-        scale = self.attn_scale.float()
+        scale = self.attn_scale.to(dtype)
         if scale.numel() == 1:
-            return None, float(scale.item()), bias * scale.to(bias.dtype)
-        qs = scale.view(1, -1, 1).expand(1, scale.numel(), S).contiguous()
+            return scale.float().reshape(1, 1, 1).expand(1, 1, S).contiguous(), bias * scale
+        qs = scale.float().view(1, -1, 1).expand(1, scale.numel(), S).contiguous()
         if per_head:
-            bias = bias * scale.to(bias.dtype).view(*([1] * (bias.dim() - 1)), -1)
+            bias = bias * scale.view(*([1] * (bias.dim() - 1)), -1)
         else:
-            bias = bias * scale.mean().to(bias.dtype)
-        return qs, 1.0, bias
-    return None, 1.0, bias
+            bias = bias * scale.mean()
+        return qs, bias
+    return None, bias
 
 
 def _patched_forward(self, hidden_states, position_embeddings=None, attention_mask=None,
@@ -149,9 +152,7 @@ def _patched_forward(self, hidden_states, position_embeddings=None, attention_ma
     Qv, Kv, Vv = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)   # (B, H, S, D) views
     if self.gate_bias is not None:
         backend = self.attn_backend_bias
-        qs, extra, bias = _phase2_q_scale_and_bias(self, B, S, q.dtype)
-        if extra != 1.0:
-            qs = torch.full((1, 1, S), extra, dtype=torch.float32, device=q.device)
+        qs, bias = _phase2_q_scale_and_bias(self, B, S, q.dtype)
         out = _attn.attention_gate_bias(Qv, Kv, Vv, bias, getattr(self, "_gate_per_head", False),
                                         backend=backend, q_row_scale=qs)
     else:

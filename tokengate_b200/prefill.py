@@ -245,8 +245,9 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
         _, hs_last = ops.add_rmsnorm(h_last, delta[rows, last_valid], inner.norm.weight,
                                      float(inner.norm.variance_epsilon))
     else:
-        gate_bias = bias_row.float()
-        set_gate_bias_for_layers(model, gate_layer + 1, n_layers, gate_bias, per_head=False)
+        # the bias in the model dtype, scaled there by an attention scale as the
+        # reference's is; _bias_bhs widens it to fp32 for the kernel
+        set_gate_bias_for_layers(model, gate_layer + 1, n_layers, bias_row, per_head=False)
         attn_scale = gate.attn_scale_eff() if has_attn_scale else None
         set_attn_scale_for_layers(model, gate_layer + 1, n_layers, attn_scale)
         for i in range(gate_layer + 1, n_layers):
