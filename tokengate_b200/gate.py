@@ -50,7 +50,14 @@ def readout_vector(gate, hidden_size: int, device) -> torch.Tensor:
     w = ro.weight.detach().reshape(-1)
     if w.numel() != hidden_size:
         raise ValueError(f"gate readout has {w.numel()} inputs, model hidden size is {hidden_size}")
-    return w.to(device=device, dtype=torch.float32).contiguous()
+    # cached per device and weight version: a CPU-resident gate would otherwise
+    # cost a pageable host-to-device copy (a stream synchronisation) per prefill
+    key = (str(device), w.data_ptr(), ro.weight._version)
+    cached = getattr(gate, "_tg_readout", None)
+    if cached is None or cached[0] != key:
+        cached = (key, w.to(device=device, dtype=torch.float32).contiguous())
+        gate._tg_readout = cached
+    return cached[1]
 
 
 # ----------------------------------------------------------------------------

@@ -205,6 +205,7 @@ def load_model(checkpoint: Optional[str] = None, base_model=None, gate_layer: Op
             gate = LinLogSigGate(hidden, generator=torch.Generator().manual_seed(seed + 1))
             if state is not None:
                 gate.load_state_dict(state)
+            gate = gate.to(dev)
     patch_model(model)
     set_attention_backends_for_layers(model, gate_attn)
     name = base_model if isinstance(base_model, str) else "custom"

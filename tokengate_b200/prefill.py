@@ -216,7 +216,9 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
 
     # ---- Phase 2
     pe2 = inner.rotary_emb(hs_pruned, kept_positions)
-    last_valid = torch.tensor([n - 1 for n in n_kepts], device=device)
+    # pinned source, asynchronous copy: a pageable one would synchronise the stream
+    last_valid = torch.tensor([n - 1 for n in n_kepts], dtype=torch.long,
+                              pin_memory=torch.cuda.is_available()).to(device, non_blocking=True)
     rows = torch.arange(B, device=device)
     if e2e:
         cos2, sin2 = pe2
