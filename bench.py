@@ -29,6 +29,9 @@ Reported (one JSON line from rank 0):
   --impl reference times that CPU implementation alone (rank 0), the
   reference arm: the reference's path is Python and CUDA code that cannot be
   built or shipped to the GPU box, so its CPU restatement stands in for it.
+  Phase 2 runs as one CUDA graph per shape (tokengate_b200.phase2_graph, the
+  reference's Phase-2 graph mode; bit-identical to eager launches);
+  --no-phase2-graphs launches it eagerly.
   --gate e2e runs the same workload with the finalized gate instead of the
   synthetic linear one (a seeded E2EGate: SwiGLU scoring branch cloned from
   layer 1, per-layer per-head bias, scaled-softmax query scale); the default
@@ -268,6 +271,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-phase2-graphs", action="store_true",
+                    help="launch the Phase-2 layers eagerly instead of replaying a CUDA graph")
     ap.add_argument("--gate", default="linear", choices=("linear", "e2e"),
                     help="linear: BASELINE's synthetic gate; e2e: a seeded finalized gate (E2EGate)")
     ap.add_argument("--profile-step", action="store_true",
@@ -293,6 +298,8 @@ def main():
         pg = dist
 
     tm = build_model(dev, args.gate)
+    from tokengate_b200.prefill import set_phase2_graphs
+    set_phase2_graphs(not args.no_phase2_graphs)
     vocab = tm.model.config.vocab_size
     prompt = make_prompt(1000 + rank, SEQ_LEN, vocab)
     ids_dev = prompt.to(dev)
@@ -386,6 +393,7 @@ def main():
                                "state [512, 32512), K=2000, gate layer 1",
                    "model": MODEL, "global_batch": world, "seq_len": SEQ_LEN, "K": K_KEEP,
                    "gate_layer": GATE_LAYER, "gate": args.gate,
+                   "phase2": "eager" if args.no_phase2_graphs else "cuda graph per shape",
                    "parallelism": f"request replicas x{world}",
                    "l2": "working set > L2 (3.4 GB weights, ~1 GB activations per step); no flush"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,

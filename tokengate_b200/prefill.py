@@ -52,6 +52,18 @@ def set_phase2_bucket(n: Optional[int]) -> None:
     _PHASE2_BUCKET = None if n is None else int(n)
 
 
+# Phase 2 of the fused path through one CUDA graph per shape (tokengate_b200.
+# phase2_graph; the reference's _PHASE2_GRAPHS mode, gate_forward.py:531-546,
+# :1528-1530). Off by default: the returned cache then aliases the graph's
+# buffers until the next prefill of the same shape.
+_PHASE2_GRAPHS = False
+
+
+def set_phase2_graphs(enabled: bool) -> None:
+    global _PHASE2_GRAPHS
+    _PHASE2_GRAPHS = bool(enabled)
+
+
 # rows per scoring-branch GEMM: bounds the [gate | up] workspace (rows x 2*inter bf16)
 _BRANCH_CHUNK = 32768
 
@@ -220,7 +232,21 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
     last_valid = torch.tensor([n - 1 for n in n_kepts], dtype=torch.long,
                               pin_memory=torch.cuda.is_available()).to(device, non_blocking=True)
     rows = torch.arange(B, device=device)
-    if e2e:
+    graphed = None
+    if fused and _PHASE2_GRAPHS:
+        from .phase2_graph import run_phase2
+        cos2, sin2 = pe2
+        if e2e:
+            graphed = run_phase2(model, fw, gate_layer, hs_pruned, cos2, sin2, bias_tab, qs_tab, cache, True)
+        else:
+            graphed = run_phase2(model, fw, gate_layer, hs_pruned, cos2, sin2,
+                                 bias_row.float().unsqueeze(1), None, cache, False)
+    if graphed is not None:
+        hs_pruned, delta = graphed
+        h_last = hs_pruned[rows, last_valid]
+        _, hs_last = ops.add_rmsnorm(h_last, delta[rows, last_valid], inner.norm.weight,
+                                     float(inner.norm.variance_epsilon))
+    elif e2e:
         cos2, sin2 = pe2
         # Phase-2 entry: the gate layer's own MLP on the kept rows (zero pad rows stay zero)
         _, x2p = ops.add_rmsnorm(hs_pruned, None, fw[gate_layer].post_w, fw[gate_layer].eps)

@@ -104,6 +104,10 @@ def main(argv=None):
     ap.add_argument("--k", default="100,500,2000,all")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=1, help="warm-up batches per K (not timed)")
+    ap.add_argument("--gate", default="linear", choices=("linear", "e2e"),
+                    help="linear: the synthetic log-sigmoid gate; e2e: a seeded finalized gate")
+    ap.add_argument("--no-phase2-graphs", action="store_true",
+                    help="launch the Phase-2 layers eagerly instead of replaying a CUDA graph per shape")
     a = ap.parse_args(argv)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -117,7 +121,10 @@ def main(argv=None):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=dev)
 
     from .inference import load_model
-    tm = load_model(base_model=a.model, gate_layer=a.gate_layer, device=dev, seed=0)
+    tm = load_model(base_model=a.model, gate_layer=a.gate_layer, device=dev, seed=0,
+                    gate="e2e" if a.gate == "e2e" else None)
+    from .prefill import set_phase2_graphs
+    set_phase2_graphs(not a.no_phase2_graphs)
     s0, s1 = (int(x) for x in a.state.split(","))
     reqs = make_requests(a.requests, a.seq, tm.model.config.vocab_size, s0, s1)
     mine = shard_requests(a.requests, world, rank)
@@ -143,7 +150,8 @@ def main(argv=None):
         wall = time.perf_counter() - t0
         recs, wall = gather_records(recs, wall)
         summ = summarize(recs, wall)
-        summ.update(K=ks, n_gpus=world, batch=a.batch, seq=a.seq, model=a.model)
+        summ.update(K=ks, n_gpus=world, batch=a.batch, seq=a.seq, model=a.model, gate=a.gate,
+                    phase2="eager" if a.no_phase2_graphs else "cuda graph per shape")
         results.append(summ)
         if rank == 0:
             print(json.dumps(summ), flush=True)
