@@ -118,65 +118,90 @@ struct QkRopeParams {
   float eps;
 };
 
-// One half-warp per (row, head): lane l of the half holds elements 8l..8l+7
-// (16-byte loads), its rotate-half partner elements (d +- 64) live in lane
-// l ^ 8; each half-warp keeps two heads in flight per iteration.
-__device__ __forceinline__ void qk_head(const QkRopeParams& p, int64_t item, int hl, bool active) {
+// One half-warp per (row, head): lane l of the half holds elements 4l..4l+3
+// and their rotate-half partners 64+4l..64+4l+3 (two 8-byte loads), so the
+// rotation needs no exchange between lanes; only the sum of squares is
+// reduced across the half. Each half-warp works on two heads per iteration,
+// with every load of both issued before any arithmetic.
+struct QkItem {
+  uint2 xl, xh, wl, wh, cl, ch, sl, sh;
+  __nv_bfloat16* base;
+  bool active;
+};
+
+__device__ __forceinline__ void qk_load(const QkRopeParams& p, int64_t item, int hl, bool active, QkItem& it) {
   const int heads = p.n_q + p.n_k;
-  const int64_t row = item / heads;
-  const int hd = (int)(item - row * heads);
+  const int64_t row = active ? item / heads : 0;
+  const int hd = active ? (int)(item - row * heads) : 0;
   const bool is_q = hd < p.n_q;
   const __nv_bfloat16* w = is_q ? p.q_w : p.k_w;
-  __nv_bfloat16* base = is_q ? p.q + row * p.ld_q + (int64_t)hd * 128
-                             : p.k + row * p.ld_k + (int64_t)(hd - p.n_q) * 128;
-  uint4* xp = reinterpret_cast<uint4*>(base) + hl;
-  uint4 xv = make_uint4(0u, 0u, 0u, 0u), cv = xv, sv = xv, wv = xv;
+  it.base = is_q ? p.q + row * p.ld_q + (int64_t)hd * 128 : p.k + row * p.ld_k + (int64_t)(hd - p.n_q) * 128;
+  it.active = active;
+  const uint2 z = make_uint2(0u, 0u);
+  it.xl = it.xh = it.wl = it.wh = it.cl = it.ch = it.sl = it.sh = z;
   if (active) {
     const int64_t b = row / p.seq, s = row - b * p.seq;
-    xv = *xp;
-    wv = __ldg(reinterpret_cast<const uint4*>(w) + hl);
-    cv = __ldg(reinterpret_cast<const uint4*>(p.cos + b * p.cs_sb + s * p.cs_ss) + hl);
-    sv = __ldg(reinterpret_cast<const uint4*>(p.sin + b * p.cs_sb + s * p.cs_ss) + hl);
+    const uint2* xp = reinterpret_cast<const uint2*>(it.base);
+    it.xl = xp[hl];
+    it.xh = xp[16 + hl];
+    const uint2* wp = reinterpret_cast<const uint2*>(w);
+    it.wl = __ldg(wp + hl);
+    it.wh = __ldg(wp + 16 + hl);
+    const uint2* cp = reinterpret_cast<const uint2*>(p.cos + b * p.cs_sb + s * p.cs_ss);
+    const uint2* sp = reinterpret_cast<const uint2*>(p.sin + b * p.cs_sb + s * p.cs_ss);
+    it.cl = __ldg(cp + hl);
+    it.ch = __ldg(cp + 16 + hl);
+    it.sl = __ldg(sp + hl);
+    it.sh = __ldg(sp + 16 + hl);
   }
-  const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
-  float x[8];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    x[2 * e] = bf16_lo(xw[e]);
-    x[2 * e + 1] = bf16_hi(xw[e]);
-  }
+}
+
+__device__ __forceinline__ float qk_sumsq(const QkItem& it) {
+  const uint32_t v[4] = {it.xl.x, it.xl.y, it.xh.x, it.xh.y};
   float ss = 0.f;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
-#pragma unroll
-  for (int off = 8; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);  // within the half
-  const float inv = rsqrtf(ss * (1.f / 128.f) + p.eps);
-  const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
-  const uint32_t* cw = reinterpret_cast<const uint32_t*>(&cv);
-  const uint32_t* sw = reinterpret_cast<const uint32_t*>(&sv);
-  float y[8];
-#pragma unroll
   for (int e = 0; e < 4; ++e) {
-    y[2 * e] = round_bf16(bf16_lo(ww[e]) * round_bf16(x[2 * e] * inv));
-    y[2 * e + 1] = round_bf16(bf16_hi(ww[e]) * round_bf16(x[2 * e + 1] * inv));
+    const float a = bf16_lo(v[e]), c = bf16_hi(v[e]);
+    ss = fmaf(a, a, ss);
+    ss = fmaf(c, c, ss);
   }
-  uint4 ov;
-  uint32_t* ow = reinterpret_cast<uint32_t*>(&ov);
+  return ss;
+}
+
+__device__ __forceinline__ void qk_finish(const QkRopeParams& p, const QkItem& it, float ss, int hl) {
+  const float inv = rsqrtf(ss * (1.f / 128.f) + p.eps);
+  const uint32_t xl[2] = {it.xl.x, it.xl.y}, xh[2] = {it.xh.x, it.xh.y};
+  const uint32_t wl[2] = {it.wl.x, it.wl.y}, wh[2] = {it.wh.x, it.wh.y};
+  const uint32_t cl[2] = {it.cl.x, it.cl.y}, ch[2] = {it.ch.x, it.ch.y};
+  const uint32_t sl[2] = {it.sl.x, it.sl.y}, sh[2] = {it.sh.x, it.sh.y};
+  uint32_t ol[2], oh[2];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    float o2[2];
+  for (int e = 0; e < 2; ++e) {
+    float lo[2], hi[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const float yy = y[2 * e + u];
-      const float partner = __shfl_xor_sync(0xffffffffu, yy, 8);
-      const float rot = hl < 8 ? -partner : partner;   // rotate_half: [-x2, x1]
-      const float c = u ? bf16_hi(cw[e]) : bf16_lo(cw[e]);
-      const float sn = u ? bf16_hi(sw[e]) : bf16_lo(sw[e]);
-      o2[u] = round_bf16(round_bf16(yy * c) + round_bf16(rot * sn));
+      const float xa = u ? bf16_hi(xl[e]) : bf16_lo(xl[e]);   // element d (< 64)
+      const float xb = u ? bf16_hi(xh[e]) : bf16_lo(xh[e]);   // element d + 64
+      const float wa = u ? bf16_hi(wl[e]) : bf16_lo(wl[e]);
+      const float wb = u ? bf16_hi(wh[e]) : bf16_lo(wh[e]);
+      const float ya = round_bf16(wa * round_bf16(xa * inv));
+      const float yb = round_bf16(wb * round_bf16(xb * inv));
+      const float ca = u ? bf16_hi(cl[e]) : bf16_lo(cl[e]);
+      const float cb = u ? bf16_hi(ch[e]) : bf16_lo(ch[e]);
+      const float sa = u ? bf16_hi(sl[e]) : bf16_lo(sl[e]);
+      const float sb = u ? bf16_hi(sh[e]) : bf16_lo(sh[e]);
+      // rotate_half: [-x2, x1]
+      lo[u] = round_bf16(round_bf16(ya * ca) + round_bf16(-yb * sa));
+      hi[u] = round_bf16(round_bf16(yb * cb) + round_bf16(ya * sb));
     }
-    ow[e] = pack_bf16x2(o2[0], o2[1]);
+    ol[e] = pack_bf16x2(lo[0], lo[1]);
+    oh[e] = pack_bf16x2(hi[0], hi[1]);
   }
-  if (active) *xp = ov;
+  if (it.active) {
+    uint2* xp = reinterpret_cast<uint2*>(it.base);
+    xp[hl] = make_uint2(ol[0], ol[1]);
+    xp[16 + hl] = make_uint2(oh[0], oh[1]);
+  }
 }
 
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkRopeParams p) {
@@ -190,8 +215,17 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkRopeParams p)
   for (int64_t base = warp_first; base < total; base += 2 * n_halves) {
     const int64_t i0 = base + (half_global & 1);
     const int64_t i1 = i0 + n_halves;
-    qk_head(p, i0, hl, i0 < total);
-    qk_head(p, i1, hl, i1 < total);
+    QkItem a, b;
+    qk_load(p, i0, hl, i0 < total, a);
+    qk_load(p, i1, hl, i1 < total, b);
+    float sa = qk_sumsq(a), sb = qk_sumsq(b);
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) {  // within the half
+      sa += __shfl_xor_sync(0xffffffffu, sa, off);
+      sb += __shfl_xor_sync(0xffffffffu, sb, off);
+    }
+    qk_finish(p, a, sa, hl);
+    qk_finish(p, b, sb, hl);
   }
 }
 
