@@ -138,6 +138,23 @@ def test_attention_large_bias_range(cuda):
     _check_attn(q, k, v, bias2, causal=True)
 
 
+def test_attention_max_outgrows_running_max(cuda):
+    """Key blocks whose logits exceed every earlier block's by far: a steep
+    ramp (each 128-key block ~25 above the last, so p would pass 2^16 and the
+    polynomial exp2's clamp) and one key 120 above the rest (2^173: inf on
+    the MUFU), in both bias templates."""
+    q, k, v = _rand_qkv(1, 1024, 1024, 2, 1, seed=23, dev=cuda)
+    ramp = torch.linspace(-100, 100, 1024).view(1, 1, 1024).to(cuda)
+    _check_attn(q, k, v, ramp, causal=True)
+    spike = torch.zeros(1, 1, 1024)
+    spike[..., 700] = 120.0
+    _check_attn(q, k, v, spike.to(cuda), causal=True)
+    # no-bias template: the same growth carried by the keys themselves
+    k2 = k.clone()
+    k2[:, 640:768] = (q[:, 640:768].float().mean(dim=2, keepdim=True) * 6).to(torch.bfloat16)
+    _check_attn(q, k2, v, None, causal=True)
+
+
 def test_attention_rejects(cuda):
     q, k, v = _rand_qkv(1, 64, 64, 2, 1, seed=1, dev=cuda)
     with pytest.raises(TokenGateUnsupportedError):

@@ -18,14 +18,14 @@
 //    from the fp32 bias in global memory;
 //  * warp 9 issues tcgen05.mma (M=128, N=128, K=16 steps): S_t = Q_t K^T
 //    (+ bias step) into TMEM, then O_t += P_t V with P read straight from
-//    TMEM (it overwrites the first 64 columns of S_t as packed bf16 pairs);
+//    TMEM (it overwrites the last 64 columns of S_t as packed bf16 pairs);
 //  * warps 0-3 / 4-7 are the softmax warpgroups of tile 0 / tile 1: one TMEM
-//    lane (= one query row) per thread, the 128-key row in registers, a
-//    3-input max over the raw logits, p = 2^(S*scale*log2e - m) with one
-//    packed FFMA2 per pair and exp2 on the MUFU. The running max is only
-//    moved (and O rescaled in TMEM) when it grows by more than 2^8, so
-//    rescales are rare; numerator and denominator share the stale max, so
-//    the result is exact.
+//    lane (= one query row) per thread, the 128-key row in registers,
+//    p = 2^(S*scale*log2e - m) with one packed FFMA2 per pair and exp2 on the
+//    MUFU. The running max m comes from the first key block's row max; later
+//    blocks use it as it is (no max pass) and only take their true max, move
+//    m and rescale O in TMEM when their row sum shows p above 2^16. Numerator
+//    and denominator share the stale max, so the result is exact.
 //  * TMEM: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512) columns.
 //
 // Issue order of the MMA warp per key block j (tile 0, tile 1):
@@ -48,6 +48,7 @@ constexpr int kMmaWarp = 9;
 constexpr int kAttnTileBytes = kAttnBM * kAttnD * 2;  // 32 KB: one Q/K/V tile
 constexpr int kAttnHalfBytes = kAttnTileBytes / 2;    // 16 KB: 64 columns (one TMA box)
 constexpr int kExtBytes = 128 * 32;                   // 4 KB: 128 rows x 16 bf16 extension
+constexpr uint32_t kAttnPCol = 64;  // P_t (packed bf16 pairs) lives in columns [64, 128) of S_t
 
 // dynamic shared memory layout (offsets from a 1024-byte aligned base)
 constexpr int kSmQ = 0;                                  // 2 tiles
@@ -60,7 +61,9 @@ constexpr int kNumBars = 17;
 
 // pairs q (0..31 per 64-key half) with (q & kAttnPolyMask) == kAttnPolyMask take
 // exp2 on the FMA pipe (degree-3 polynomial) instead of the MUFU; a mask of
-// -1 keeps every exp2 on the MUFU
+// -1 (the default) keeps every exp2 on the MUFU. Moving 1/8 or 1/4 of the
+// pairs to the FMA pipe measured no faster on B200 (and slower with the key
+// bias, whose variant then spills).
 #ifndef TG_ATTN_POLY_MASK
 #define TG_ATTN_POLY_MASK -1
 #endif
@@ -181,6 +184,59 @@ __device__ __forceinline__ uint32_t split_bf16x2(float v) {
   return (uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(lo) << 16);
 }
 
+// row max of the 128 raw logits a thread holds: eight independent 3-input
+// max chains (their latency, not the instruction count, bounds this step),
+// then a short tree
+__device__ __forceinline__ float attn_row_max(const uint32_t (&sv)[128]) {
+  float mxa[8];
+#pragma unroll
+  for (int a = 0; a < 8; ++a) mxa[a] = fmaxf(__uint_as_float(sv[2 * a]), __uint_as_float(sv[2 * a + 1]));
+#pragma unroll
+  for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+      mxa[a] = fmax3(mxa[a], __uint_as_float(sv[c + 2 * a]), __uint_as_float(sv[c + 2 * a + 1]));
+  }
+  return fmaxf(fmax3(mxa[0], mxa[1], mxa[2]), fmaxf(fmax3(mxa[3], mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+}
+
+// p = 2^(S*c2 - m) for one row of 128 logits: one FFMA2 per pair and exp2 on
+// the MUFU, except for the pairs the poly mask sends to the FMA pipe (clamped
+// polynomial). P goes to TMEM as packed bf16 pairs, 32 keys per store
+// (asynchronous stores: the caller waits before publishing); returns the row
+// sum of the fp32 p.
+__device__ __forceinline__ float attn_exp_store(const uint32_t (&sv)[128], float c2, float m, uint32_t tS) {
+  const float2 c22 = make_float2(c2, c2);
+  const float2 negm = make_float2(-m, -m);
+  const float a_sat = c2 * (1.f / kPolyRange);
+  const float b_sat = (-m - kPolyLo) * (1.f / kPolyRange);
+  float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                  make_float2(0.f, 0.f)};
+#pragma unroll
+  for (int qt = 0; qt < 4; ++qt) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int qq = 0; qq < 16; ++qq) {
+      const int q = (qt & 1) * 16 + qq;  // pair index inside its 64-key half
+      const int c = qt * 32 + 2 * qq;
+      float2 pp;
+      if (kAttnPolyMask >= 0 && (q & kAttnPolyMask) == kAttnPolyMask) {
+        pp = exp2_poly2_sat(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), a_sat, b_sat);
+      } else {
+        const float2 d = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
+                                    c22, negm);
+        pp.x = ex2_approx(d.x);
+        pp.y = ex2_approx(d.y);
+      }
+      ls[q & 3] = __fadd2_rn(ls[q & 3], pp);
+      pk[qq] = pack_bf16x2(pp.x, pp.y);
+    }
+    tmem_st16_async(tS + kAttnPCol + qt * 16, pk);
+  }
+  const float2 lsum = __fadd2_rn(__fadd2_rn(ls[0], ls[1]), __fadd2_rn(ls[2], ls[3]));
+  return lsum.x + lsum.y;
+}
+
 template <bool kHasBias>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     keybias_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -248,11 +304,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   // Register split (launch: 384 threads x 168 = 64512): the two softmax
-  // warpgroups take 216 each, the producer/MMA warpgroup keeps 72:
-  // 2*128*216 + 128*72 = 64512 (no spills in either role). Each role's code
-  // is dominated by its own setmaxnreg so the allocator gives it that budget.
+  // warpgroups take 192 each, the producer/MMA warpgroup keeps 120:
+  // 2*128*192 + 128*120 = 64512 (no spills in either role or either bias
+  // variant; the producer's bias-extension code needs more than 72). Each
+  // role's code is dominated by its own setmaxnreg so the allocator gives it
+  // that budget.
   if (warp >= kProducerWarp) {
-  setmaxnreg_dec<72>();
+  setmaxnreg_dec<120>();
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -355,7 +413,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t va = sV + s * kAttnTileBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          umma_ts(tmem + 256u + t * 128u, tmem + t * 128u + kk * 8,
+          umma_ts(tmem + 256u + t * 128u, tmem + t * 128u + kAttnPCol + kk * 8,
                   umma_desc_sw128(va + kk * 2048, kAttnHalfBytes, 1024),
                   kIdescPV, (acc || kk > 0) ? 1u : 0u);
         }
@@ -433,7 +491,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncwarp();
   }
   } else {
-    setmaxnreg_inc<216>();
+    setmaxnreg_inc<192>();
     // ------------------------------------------------------------ softmax
     const int t = warp >> 2;
     const int sub = warp & 3;
@@ -476,7 +534,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
 
     const float c2 = p.scale_log2;   // raw logit -> log2 units
-    const float2 c22 = make_float2(c2, c2);
     float m_run = -INFINITY;         // running max, log2 units
     float l_run = 0.f;
     const int diag_blk = p.causal ? (me.m0 / kAttnBN) : -1;
@@ -491,43 +548,57 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_ld128(tS, sv);
 
       // masks: causal edge (keys past the query row) and keys past Sk
-      if (j == diag_blk || (!p.causal && j == last_blk && tail_keys < kAttnBN)) {
-        const int lim = (j == diag_blk) ? r : tail_keys - 1;
+      const bool masked = j == diag_blk || (!p.causal && j == last_blk && tail_keys < kAttnBN);
+      const int lim = (j == diag_blk) ? r : tail_keys - 1;
+      if (masked) {
 #pragma unroll
         for (int c = 0; c < 128; ++c)
           if (c > lim) sv[c] = __float_as_uint(-INFINITY);
       }
-      // row max: eight independent 3-input-max chains (the chains' latency,
-      // not the instruction count, bounds this step), then a short tree
-      float mxa[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) mxa[a] = fmaxf(__uint_as_float(sv[2 * a]), __uint_as_float(sv[2 * a + 1]));
-#pragma unroll
-      for (int c = 16; c < 128; c += 16) {
-#pragma unroll
-        for (int a = 0; a < 8; ++a)
-          mxa[a] = fmax3(mxa[a], __uint_as_float(sv[c + 2 * a]), __uint_as_float(sv[c + 2 * a + 1]));
-      }
-      const float mx = fmaxf(fmax3(mxa[0], mxa[1], mxa[2]), fmaxf(fmax3(mxa[3], mxa[4], mxa[5]),
-                                                                   fmaxf(mxa[6], mxa[7]))) * c2;
+      // block 0 sets the running max from its true row max (3-input max
+      // chains); later blocks start optimistically from the running max and
+      // only take the true max when their row sum shows that the logits
+      // outgrew it (below)
+      if (j == 0) m_run = attn_row_max(sv) * c2;
+      float msub = (m_run == -INFINITY) ? 0.f : m_run;
+      float lsum = attn_exp_store(sv, c2, msub, tS);
 
-      // lazy max: move it (and rescale O) only when it grows by more than 8 in
-      // log2 units; O is stable here because S_t(j) completing implies the
-      // P_t(j-1) V MMA, issued earlier, completed too.
-      const float m_new = fmaxf(m_run, mx);
-      bool need = false;
-      float alpha = 1.f;
-      if (j == 0) {
-        m_run = m_new;
-      } else if (m_new > m_run + 8.0f) {
-        need = true;
-        alpha = ex2_approx(m_run - m_new);
+      // a row whose logits exceed the running max by more than ~16 in log2
+      // units has a row sum above 2^16 (or inf): the warp then moves the max
+      // for those rows, rescales O and recomputes P. Below that bound P and
+      // the row sum carry the factor 2^(m_true - m_run) <= 2^16 in both the
+      // numerator and the denominator, so the result is unchanged. O is
+      // stable here because S_t(j) completing implies the P_t(j-1) V MMA,
+      // issued earlier, completed too; P is only published after this.
+      const bool grew = !(lsum <= 65536.f);
+      if (__any_sync(0xffffffffu, grew)) {
+        // P overwrote the logits of keys 64..127 in TMEM (still in registers:
+        // they were consumed last); keys 0..63 are read back from TMEM
+        {
+          uint32_t h0[32], h1[32];
+          tmem_ld32(tS, h0);
+          tmem_ld32(tS + 32, h1);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            sv[e] = h0[e];
+            sv[32 + e] = h1[e];
+          }
+          if (masked) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+              if (c > lim) sv[c] = __float_as_uint(-INFINITY);
+          }
+        }
+        const float m_new = fmaxf(m_run, attn_row_max(sv) * c2);
+        float alpha = 1.f;
+        if (grew && m_new > m_run) {
+          alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - m_new);
+          m_run = m_new;
+        }
         l_run *= alpha;
-        m_run = m_new;
-      }
-      // O must be rescaled before this block's first P half is published
-      // (the P V MMA accumulates into it)
-      if (__any_sync(0xffffffffu, need)) {
+        tmem_wait_st();  // the optimistic P stores land before they are replaced
+        msub = (m_run == -INFINITY) ? 0.f : m_run;
+        lsum = attn_exp_store(sv, c2, msub, tS);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -537,40 +608,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_st32(tO + c * 32, o);
         }
       }
-      const float msub = (m_run == -INFINITY) ? 0.f : m_run;
-      const float2 negm = make_float2(-msub, -msub);
-
-      // p = 2^(S*c2 - m): one FFMA2 per pair, exp2 on the MUFU except for the
-      // pairs the poly mask assigns to the FMA pipe; P is stored as packed
-      // bf16 pairs in two 64-key halves and published once both are in TMEM
-      float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                      make_float2(0.f, 0.f)};
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int c = half * 64 + 2 * q;
-          const float2 d = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
-                                      c22, negm);
-          float2 pp;
-          if (kAttnPolyMask >= 0 && (q & kAttnPolyMask) == kAttnPolyMask) {
-            pp = exp2_poly2_lean(d);
-          } else {
-            pp.x = ex2_approx(d.x);
-            pp.y = ex2_approx(d.y);
-          }
-          ls[q & 3] = __fadd2_rn(ls[q & 3], pp);
-          pk[q] = pack_bf16x2(pp.x, pp.y);
-        }
-        tmem_st32_async(tS + half * 32, pk);
-      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_P_FULL + t));
-      const float2 lsum = __fadd2_rn(__fadd2_rn(ls[0], ls[1]), __fadd2_rn(ls[2], ls[3]));
-      l_run += lsum.x + lsum.y;
+      l_run += lsum;
     }
 
     if (ok && me.nblk > 0) {

@@ -235,6 +235,10 @@ __device__ __forceinline__ void tmem_st32_async(uint32_t taddr, const uint32_t (
   asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
                :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]) : "memory");
 }
+__device__ __forceinline__ void tmem_st16_async(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
+               :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]) : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
@@ -260,17 +264,25 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for two values, x <= 64, on the FMA pipe: one lower clamp (at -126,
-// where 2^x is below every bf16 P that matters and the exponent field stays
-// in range), rounding to n + f with |f| <= 1/2 by the 1.5*2^23 shifter, 2^f
-// from a degree-3 polynomial fitted on [-1/2, 1/2] (relative minimax,
-// 7.5e-5), and n added to the exponent field with one shift-add per value.
-__device__ __forceinline__ float2 exp2_poly2_lean(float2 x) {
-  x.x = fmaxf(x.x, -126.f);
-  x.y = fmaxf(x.y, -126.f);
-  const float2 shifter = make_float2(12582912.f, 12582912.f);
-  const float2 t = __fadd2_rn(x, shifter);
-  const float2 f = __fadd2_rn(x, __fadd2_rn(shifter, make_float2(-t.x, -t.y)));
+// 2^x for two logits s, x = s*c - m clamped to [kPolyLo, kPolyLo + kPolyRange],
+// on the FMA pipe. The clamp is the FMA's saturation: u = sat(s*a + b) with
+// a = c / range, b = (-m - lo) / range, then x = u*range + lo (at -126 2^x is
+// below every bf16 P that matters and the exponent field stays in range; the
+// upper end, 2^32, is far above any value the caller accepts, so a logit that
+// outgrew m shows as a large row sum instead of a wrapped exponent). x is
+// rounded to n + f with |f| <= 1/2 by the 1.5*2^23 shifter, 2^f comes from a
+// degree-3 polynomial fitted on [-1/2, 1/2] (relative minimax, 7.5e-5), and n
+// is added to the exponent field with one shift-add per value.
+constexpr float kPolyLo = -126.f;
+constexpr float kPolyRange = 158.f;
+__device__ __forceinline__ float2 exp2_poly2_sat(float sx, float sy, float a, float b) {
+  float2 u;
+  u.x = __saturatef(__fmaf_rn(sx, a, b));
+  u.y = __saturatef(__fmaf_rn(sy, a, b));
+  const float2 rng = make_float2(kPolyRange, kPolyRange);
+  const float2 c = make_float2(12582912.f + kPolyLo, 12582912.f + kPolyLo);  // shifter + lo, exact
+  const float2 t = __ffma2_rn(u, rng, c);                                      // shifter + round(x)
+  const float2 f = __ffma2_rn(u, rng, __fadd2_rn(c, make_float2(-t.x, -t.y)));  // x - round(x)
   float2 q = __ffma2_rn(make_float2(0.05517097935f, 0.05517097935f), f,
                         make_float2(0.24260970950f, 0.24260970950f));
   q = __ffma2_rn(q, f, make_float2(0.69326096773f, 0.69326096773f));
