@@ -389,12 +389,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    // One thread issues every MMA; a tcgen05.mma occupies the issuing thread
-    // for about the time the tensor pipe needs for one 128x128x16 step, so
-    // the steady-state loop below carries nothing but the MMAs, the waits
-    // they depend on (one try_wait each when already complete) and the
-    // commits the other roles wait for.
-    if (lane == 0) {
+    // The whole warp runs this code (descriptors and control flow stay
+    // warp-uniform) and one elected lane issues each MMA and commit: issued
+    // from a warp-converged loop a tcgen05.mma costs the issuer ~25 clocks,
+    // from a single-lane branch ~49 (measured on B200), against 64 clocks of
+    // tensor-pipe time per 128x128x16 step. The steady-state loop below
+    // carries nothing but the MMAs, the waits they depend on and the commits
+    // the other roles wait for.
+    {
       constexpr uint32_t kIdescQK = umma_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t kIdescPV = umma_idesc_bf16(128, 128, 0, 1);
       auto issue_qk = [&](int t, int s) {
@@ -402,33 +404,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kAttnHalfBytes + (kk & 3) * 32;
-          umma_ss(tmem + t * 128u, umma_desc_sw128(qa + off, 16, 1024),
-                  umma_desc_sw128(ka + off, 16, 1024), kIdescQK, kk > 0);
+          if (elect_one())
+            umma_ss(tmem + t * 128u, umma_desc_sw128(qa + off, 16, 1024),
+                    umma_desc_sw128(ka + off, 16, 1024), kIdescQK, kk > 0);
         }
         if constexpr (kHasBias)
-          umma_ss(tmem + t * 128u, umma_desc_sw32(sQExt + t * kExtBytes, 16, 256),
-                  umma_desc_sw32(sKExt + s * kExtBytes, 16, 256), kIdescQK, 1u);
+          if (elect_one())
+            umma_ss(tmem + t * 128u, umma_desc_sw32(sQExt + t * kExtBytes, 16, 256),
+                    umma_desc_sw32(sKExt + s * kExtBytes, 16, 256), kIdescQK, 1u);
       };
       auto issue_pv = [&](int t, int s, bool acc) {
         const uint32_t va = sV + s * kAttnTileBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          umma_ts(tmem + 256u + t * 128u, tmem + t * 128u + kAttnPCol + kk * 8,
-                  umma_desc_sw128(va + kk * 2048, kAttnHalfBytes, 1024),
-                  kIdescPV, (acc || kk > 0) ? 1u : 0u);
+          if (elect_one())
+            umma_ts(tmem + 256u + t * 128u, tmem + t * 128u + kAttnPCol + kk * 8,
+                    umma_desc_sw128(va + kk * 2048, kAttnHalfBytes, 1024), kIdescPV,
+                    (acc || kk > 0) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait(bar(BAR_Q), 0, p.err, ERR_ATTN_Q);
-      if (ok && has_qscale) ok = mbar_wait(bar(BAR_Q_READY), 0, p.err, ERR_ATTN_Q_READY);
-      if (ok && nblk > 0) ok = mbar_wait(bar(BAR_K_FULL + 0), 0, p.err, ERR_ATTN_K_FULL);
+      bool ok = warp_wait(bar(BAR_Q), 0, p.err, ERR_ATTN_Q);
+      if (ok && has_qscale) ok = warp_wait(bar(BAR_Q_READY), 0, p.err, ERR_ATTN_Q_READY);
+      if (ok && nblk > 0) ok = warp_wait(bar(BAR_K_FULL + 0), 0, p.err, ERR_ATTN_K_FULL);
       if (ok && nblk > 0) {
         for (int t = 0; t < 2; ++t) {
           if (ti[t].nblk > 0) {
             issue_qk(t, 0);
-            umma_commit(bar(BAR_S_FULL + t));
+            if (elect_one()) umma_commit(bar(BAR_S_FULL + t));
           }
         }
-        umma_commit(bar(BAR_K_EMPTY + 0));
+        if (elect_one()) umma_commit(bar(BAR_K_EMPTY + 0));
       }
       // steady state: both tiles need blocks j and j + 1
       const int nboth = min(ti[0].nblk, ti[1].nblk) - 1;
@@ -436,57 +441,61 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (; ok && j < nboth; ++j) {
         const int s = j & 1, s1 = s ^ 1;
         const uint32_t ph = (j >> 1) & 1, ph1 = ((j + 1) >> 1) & 1, pp = j & 1;
-        if (!mbar_wait(bar(BAR_V_FULL + s), ph, p.err, ERR_ATTN_V_FULL)) { ok = false; break; }
-        if (!mbar_wait(bar(BAR_P_FULL + 0), pp, p.err, ERR_ATTN_P_FULL)) { ok = false; break; }
+        if (!warp_wait(bar(BAR_V_FULL + s), ph, p.err, ERR_ATTN_V_FULL)) { ok = false; break; }
+        if (!warp_wait(bar(BAR_P_FULL + 0), pp, p.err, ERR_ATTN_P_FULL)) { ok = false; break; }
         tc_fence_after();
         issue_pv(0, s, j > 0);
-        if (!mbar_wait(bar(BAR_K_FULL + s1), ph1, p.err, ERR_ATTN_K_FULL)) { ok = false; break; }
+        if (!warp_wait(bar(BAR_K_FULL + s1), ph1, p.err, ERR_ATTN_K_FULL)) { ok = false; break; }
         issue_qk(0, s1);
-        umma_commit(bar(BAR_S_FULL + 0));
-        if (!mbar_wait(bar(BAR_P_FULL + 1), pp, p.err, ERR_ATTN_P_FULL)) { ok = false; break; }
+        if (elect_one()) umma_commit(bar(BAR_S_FULL + 0));
+        if (!warp_wait(bar(BAR_P_FULL + 1), pp, p.err, ERR_ATTN_P_FULL)) { ok = false; break; }
         tc_fence_after();
         issue_pv(1, s, j > 0);
-        umma_commit(bar(BAR_V_EMPTY + s));
+        if (elect_one()) umma_commit(bar(BAR_V_EMPTY + s));
         issue_qk(1, s1);
-        umma_commit(bar(BAR_S_FULL + 1));
-        umma_commit(bar(BAR_K_EMPTY + s1));
+        if (elect_one()) umma_commit(bar(BAR_S_FULL + 1));
+        if (elect_one()) umma_commit(bar(BAR_K_EMPTY + s1));
       }
       // tail: the blocks where one tile has finished or no next block exists
       for (; ok && j < nblk; ++j) {
         const int s = j & 1, s1 = s ^ 1;
         const bool more = (j + 1) < nblk;
-        if (!mbar_wait(bar(BAR_V_FULL + s), (j >> 1) & 1, p.err, ERR_ATTN_V_FULL)) break;
+        if (!warp_wait(bar(BAR_V_FULL + s), (j >> 1) & 1, p.err, ERR_ATTN_V_FULL)) break;
         if (j < ti[0].nblk) {
-          if (!mbar_wait(bar(BAR_P_FULL + 0), j & 1, p.err, ERR_ATTN_P_FULL)) break;
+          if (!warp_wait(bar(BAR_P_FULL + 0), j & 1, p.err, ERR_ATTN_P_FULL)) break;
           tc_fence_after();
           issue_pv(0, s, j > 0);
-          if (j == ti[0].nblk - 1) umma_commit(bar(BAR_O_FULL + 0));
+          if (j == ti[0].nblk - 1) {
+            if (elect_one()) umma_commit(bar(BAR_O_FULL + 0));
+          }
         }
         if (more) {
-          if (!mbar_wait(bar(BAR_K_FULL + s1), ((j + 1) >> 1) & 1, p.err, ERR_ATTN_K_FULL)) break;
+          if (!warp_wait(bar(BAR_K_FULL + s1), ((j + 1) >> 1) & 1, p.err, ERR_ATTN_K_FULL)) break;
           if (j + 1 < ti[0].nblk) {
             issue_qk(0, s1);
-            umma_commit(bar(BAR_S_FULL + 0));
+            if (elect_one()) umma_commit(bar(BAR_S_FULL + 0));
           }
         }
         if (j < ti[1].nblk) {
-          if (!mbar_wait(bar(BAR_P_FULL + 1), j & 1, p.err, ERR_ATTN_P_FULL)) break;
+          if (!warp_wait(bar(BAR_P_FULL + 1), j & 1, p.err, ERR_ATTN_P_FULL)) break;
           tc_fence_after();
           issue_pv(1, s, j > 0);
-          if (j == ti[1].nblk - 1) umma_commit(bar(BAR_O_FULL + 1));
+          if (j == ti[1].nblk - 1) {
+            if (elect_one()) umma_commit(bar(BAR_O_FULL + 1));
+          }
         }
-        umma_commit(bar(BAR_V_EMPTY + s));
+        if (elect_one()) umma_commit(bar(BAR_V_EMPTY + s));
         if (more) {
           if (j + 1 < ti[1].nblk) {
             issue_qk(1, s1);
-            umma_commit(bar(BAR_S_FULL + 1));
+            if (elect_one()) umma_commit(bar(BAR_S_FULL + 1));
           }
-          umma_commit(bar(BAR_K_EMPTY + s1));
+          if (elect_one()) umma_commit(bar(BAR_K_EMPTY + s1));
         }
       }
       // every MMA issued so far has completed before TMEM is released
-      umma_commit(bar(BAR_MMA_DONE));
-      mbar_wait(bar(BAR_MMA_DONE), 0, p.err, ERR_ATTN_DRAIN);
+      if (elect_one()) umma_commit(bar(BAR_MMA_DONE));
+      warp_wait(bar(BAR_MMA_DONE), 0, p.err, ERR_ATTN_DRAIN);
     }
     __syncwarp();
   }
