@@ -118,46 +118,65 @@ struct QkRopeParams {
   float eps;
 };
 
-// One half-warp per (row, head): lane l of the half holds elements 4l..4l+3
-// and their rotate-half partners 64+4l..64+4l+3 (two 8-byte loads), so the
-// rotation needs no exchange between lanes; only the sum of squares is
-// reduced across the half. Each half-warp works on two heads per iteration,
-// with every load of both issued before any arithmetic.
-struct QkItem {
-  uint2 xl, xh, wl, wh, cl, ch, sl, sh;
-  __nv_bfloat16* base;
-  bool active;
+// One warp per row: the row's cos / sin and the two norm gains are loaded
+// once, then each half-warp takes every other head of the row, up to
+// kQkBatch heads per half with every load issued before any arithmetic. Lane
+// l of a half holds elements 4l..4l+3 of its head and their rotate-half
+// partners 64+4l..64+4l+3 (two 8-byte loads), so the rotation needs no
+// exchange between lanes; only the sum of squares is reduced across the half.
+constexpr int kQkBatch = 4;
+
+struct QkRow {
+  uint2 cl, ch, sl, sh;  // cos / sin of this lane's elements
 };
 
-__device__ __forceinline__ void qk_load(const QkRopeParams& p, int64_t item, int hl, bool active, QkItem& it) {
-  const int heads = p.n_q + p.n_k;
-  const int64_t row = active ? item / heads : 0;
-  const int hd = active ? (int)(item - row * heads) : 0;
-  const bool is_q = hd < p.n_q;
-  const __nv_bfloat16* w = is_q ? p.q_w : p.k_w;
-  it.base = is_q ? p.q + row * p.ld_q + (int64_t)hd * 128 : p.k + row * p.ld_k + (int64_t)(hd - p.n_q) * 128;
-  it.active = active;
-  const uint2 z = make_uint2(0u, 0u);
-  it.xl = it.xh = it.wl = it.wh = it.cl = it.ch = it.sl = it.sh = z;
-  if (active) {
-    const int64_t b = row / p.seq, s = row - b * p.seq;
-    const uint2* xp = reinterpret_cast<const uint2*>(it.base);
-    it.xl = xp[hl];
-    it.xh = xp[16 + hl];
-    const uint2* wp = reinterpret_cast<const uint2*>(w);
-    it.wl = __ldg(wp + hl);
-    it.wh = __ldg(wp + 16 + hl);
-    const uint2* cp = reinterpret_cast<const uint2*>(p.cos + b * p.cs_sb + s * p.cs_ss);
-    const uint2* sp = reinterpret_cast<const uint2*>(p.sin + b * p.cs_sb + s * p.cs_ss);
-    it.cl = __ldg(cp + hl);
-    it.ch = __ldg(cp + 16 + hl);
-    it.sl = __ldg(sp + hl);
-    it.sh = __ldg(sp + 16 + hl);
-  }
+// rounds two floats to bf16 with one paired conversion
+__device__ __forceinline__ void round_bf16x2(float& a, float& b) {
+  const uint32_t w = pack_bf16x2(a, b);
+  a = bf16_lo(w);
+  b = bf16_hi(w);
 }
 
-__device__ __forceinline__ float qk_sumsq(const QkItem& it) {
-  const uint32_t v[4] = {it.xl.x, it.xl.y, it.xh.x, it.xh.y};
+__device__ __forceinline__ void qk_finish(const uint2 xl2, const uint2 xh2, const uint2 wl2, const uint2 wh2,
+                                          const QkRow& cs, float ss, float eps, uint2& out_l, uint2& out_h) {
+  const float inv = rsqrtf(ss * (1.f / 128.f) + eps);
+  const uint32_t xl[2] = {xl2.x, xl2.y}, xh[2] = {xh2.x, xh2.y};
+  const uint32_t wl[2] = {wl2.x, wl2.y}, wh[2] = {wh2.x, wh2.y};
+  const uint32_t cl[2] = {cs.cl.x, cs.cl.y}, ch[2] = {cs.ch.x, cs.ch.y};
+  const uint32_t sl[2] = {cs.sl.x, cs.sl.y}, sh[2] = {cs.sh.x, cs.sh.y};
+  uint32_t ol[2], oh[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    // elements d, d + 1 (< 64) and their rotate-half partners d + 64, d + 65;
+    // every rounding point of the eager ops, two values per conversion
+    float ya0 = bf16_lo(xl[e]) * inv, ya1 = bf16_hi(xl[e]) * inv;
+    float yb0 = bf16_lo(xh[e]) * inv, yb1 = bf16_hi(xh[e]) * inv;
+    round_bf16x2(ya0, ya1);
+    round_bf16x2(yb0, yb1);
+    ya0 *= bf16_lo(wl[e]);
+    ya1 *= bf16_hi(wl[e]);
+    yb0 *= bf16_lo(wh[e]);
+    yb1 *= bf16_hi(wh[e]);
+    round_bf16x2(ya0, ya1);
+    round_bf16x2(yb0, yb1);
+    // rotate_half: [-x2, x1]
+    float pc0 = ya0 * bf16_lo(cl[e]), pc1 = ya1 * bf16_hi(cl[e]);
+    float ps0 = -yb0 * bf16_lo(sl[e]), ps1 = -yb1 * bf16_hi(sl[e]);
+    float qc0 = yb0 * bf16_lo(ch[e]), qc1 = yb1 * bf16_hi(ch[e]);
+    float qs0 = ya0 * bf16_lo(sh[e]), qs1 = ya1 * bf16_hi(sh[e]);
+    round_bf16x2(pc0, pc1);
+    round_bf16x2(ps0, ps1);
+    round_bf16x2(qc0, qc1);
+    round_bf16x2(qs0, qs1);
+    ol[e] = pack_bf16x2(pc0 + ps0, pc1 + ps1);
+    oh[e] = pack_bf16x2(qc0 + qs0, qc1 + qs1);
+  }
+  out_l = make_uint2(ol[0], ol[1]);
+  out_h = make_uint2(oh[0], oh[1]);
+}
+
+__device__ __forceinline__ float qk_sumsq(const uint2 xl, const uint2 xh) {
+  const uint32_t v[4] = {xl.x, xl.y, xh.x, xh.y};
   float ss = 0.f;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
@@ -168,64 +187,66 @@ __device__ __forceinline__ float qk_sumsq(const QkItem& it) {
   return ss;
 }
 
-__device__ __forceinline__ void qk_finish(const QkRopeParams& p, const QkItem& it, float ss, int hl) {
-  const float inv = rsqrtf(ss * (1.f / 128.f) + p.eps);
-  const uint32_t xl[2] = {it.xl.x, it.xl.y}, xh[2] = {it.xh.x, it.xh.y};
-  const uint32_t wl[2] = {it.wl.x, it.wl.y}, wh[2] = {it.wh.x, it.wh.y};
-  const uint32_t cl[2] = {it.cl.x, it.cl.y}, ch[2] = {it.ch.x, it.ch.y};
-  const uint32_t sl[2] = {it.sl.x, it.sl.y}, sh[2] = {it.sh.x, it.sh.y};
-  uint32_t ol[2], oh[2];
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    float lo[2], hi[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const float xa = u ? bf16_hi(xl[e]) : bf16_lo(xl[e]);   // element d (< 64)
-      const float xb = u ? bf16_hi(xh[e]) : bf16_lo(xh[e]);   // element d + 64
-      const float wa = u ? bf16_hi(wl[e]) : bf16_lo(wl[e]);
-      const float wb = u ? bf16_hi(wh[e]) : bf16_lo(wh[e]);
-      const float ya = round_bf16(wa * round_bf16(xa * inv));
-      const float yb = round_bf16(wb * round_bf16(xb * inv));
-      const float ca = u ? bf16_hi(cl[e]) : bf16_lo(cl[e]);
-      const float cb = u ? bf16_hi(ch[e]) : bf16_lo(ch[e]);
-      const float sa = u ? bf16_hi(sl[e]) : bf16_lo(sl[e]);
-      const float sb = u ? bf16_hi(sh[e]) : bf16_lo(sh[e]);
-      // rotate_half: [-x2, x1]
-      lo[u] = round_bf16(round_bf16(ya * ca) + round_bf16(-yb * sa));
-      hi[u] = round_bf16(round_bf16(yb * cb) + round_bf16(ya * sb));
+__global__ void __launch_bounds__(256, 3) qk_norm_rope_kernel(const QkRopeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int hl = lane & 15;    // lane inside the half-warp
+  const int half = lane >> 4;  // heads half, half + 2, half + 4, ...
+  const int64_t warp_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int heads = p.n_q + p.n_k;
+  const uint2* qwp = reinterpret_cast<const uint2*>(p.q_w);
+  const uint2* kwp = reinterpret_cast<const uint2*>(p.k_w);
+  const uint2 qwl = __ldg(qwp + hl), qwh = __ldg(qwp + 16 + hl);
+  const uint2 kwl = __ldg(kwp + hl), kwh = __ldg(kwp + 16 + hl);
+  for (int64_t row = warp_global; row < p.rows; row += n_warps) {
+    const int64_t b = row / p.seq, s = row - b * p.seq;
+    QkRow cs;
+    {
+      const uint2* cp = reinterpret_cast<const uint2*>(p.cos + b * p.cs_sb + s * p.cs_ss);
+      const uint2* sp = reinterpret_cast<const uint2*>(p.sin + b * p.cs_sb + s * p.cs_ss);
+      cs.cl = __ldg(cp + hl);
+      cs.ch = __ldg(cp + 16 + hl);
+      cs.sl = __ldg(sp + hl);
+      cs.sh = __ldg(sp + 16 + hl);
     }
-    ol[e] = pack_bf16x2(lo[0], lo[1]);
-    oh[e] = pack_bf16x2(hi[0], hi[1]);
-  }
-  if (it.active) {
-    uint2* xp = reinterpret_cast<uint2*>(it.base);
-    xp[hl] = make_uint2(ol[0], ol[1]);
-    xp[16 + hl] = make_uint2(oh[0], oh[1]);
-  }
-}
-
-__global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkRopeParams p) {
-  const int hl = threadIdx.x & 15;  // lane inside the half-warp
-  const int64_t total = p.rows * (p.n_q + p.n_k);
-  const int64_t half_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
-  const int64_t n_halves = ((int64_t)gridDim.x * blockDim.x) >> 4;
-  // two items per iteration; the loop bound is uniform across the warp
-  // (both halves iterate until every half of the warp is done)
-  const int64_t warp_first = half_global & ~int64_t(1);
-  for (int64_t base = warp_first; base < total; base += 2 * n_halves) {
-    const int64_t i0 = base + (half_global & 1);
-    const int64_t i1 = i0 + n_halves;
-    QkItem a, b;
-    qk_load(p, i0, hl, i0 < total, a);
-    qk_load(p, i1, hl, i1 < total, b);
-    float sa = qk_sumsq(a), sb = qk_sumsq(b);
+    __nv_bfloat16* qrow = p.q + row * p.ld_q;
+    __nv_bfloat16* krow = p.k + row * p.ld_k;
+    // the head loop is uniform across the warp (the shuffles need every lane)
+    for (int h0 = 0; h0 < heads; h0 += 2 * kQkBatch) {
+      uint2 xl[kQkBatch], xh[kQkBatch];
+      float ss[kQkBatch];
 #pragma unroll
-    for (int off = 8; off >= 1; off >>= 1) {  // within the half
-      sa += __shfl_xor_sync(0xffffffffu, sa, off);
-      sb += __shfl_xor_sync(0xffffffffu, sb, off);
+      for (int i = 0; i < kQkBatch; ++i) {
+        const int hd = h0 + 2 * i + half;
+        xl[i] = xh[i] = make_uint2(0u, 0u);
+        if (hd < heads) {
+          const uint2* xp = reinterpret_cast<const uint2*>(
+              hd < p.n_q ? qrow + (int64_t)hd * 128 : krow + (int64_t)(hd - p.n_q) * 128);
+          xl[i] = xp[hl];
+          xh[i] = xp[16 + hl];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kQkBatch; ++i) ss[i] = qk_sumsq(xl[i], xh[i]);
+#pragma unroll
+      for (int off = 8; off >= 1; off >>= 1) {  // within the half
+#pragma unroll
+        for (int i = 0; i < kQkBatch; ++i) ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], off);
+      }
+#pragma unroll
+      for (int i = 0; i < kQkBatch; ++i) {
+        const int hd = h0 + 2 * i + half;
+        if (hd < heads) {
+          const bool is_q = hd < p.n_q;
+          uint2 ol, oh;
+          qk_finish(xl[i], xh[i], is_q ? qwl : kwl, is_q ? qwh : kwh, cs, ss[i], p.eps, ol, oh);
+          uint2* xp = reinterpret_cast<uint2*>(is_q ? qrow + (int64_t)hd * 128
+                                                    : krow + (int64_t)(hd - p.n_q) * 128);
+          xp[hl] = ol;
+          xp[16 + hl] = oh;
+        }
+      }
     }
-    qk_finish(p, a, sa, hl);
-    qk_finish(p, b, sb, hl);
   }
 }
 
@@ -254,8 +275,9 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const SiluParams p) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float g0 = bf16_lo(g[e]), g1 = bf16_hi(g[e]);
-      const float a0 = round_bf16(g0 / (1.f + expf(-g0)));
-      const float a1 = round_bf16(g1 / (1.f + expf(-g1)));
+      float a0 = g0 / (1.f + expf(-g0));
+      float a1 = g1 / (1.f + expf(-g1));
+      round_bf16x2(a0, a1);
       o[e] = pack_bf16x2(a0 * bf16_lo(u[e]), a1 * bf16_hi(u[e]));
     }
     reinterpret_cast<uint4*>(p.out + row * p.ld_out)[c] = o4;

@@ -501,7 +501,7 @@ int tg_qk_norm_rope(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k,
   p.cs_sb = cs_sb;
   p.cs_ss = cs_ss;
   p.eps = eps;
-  const int64_t blocks = resident_blocks((rows * (n_q_heads + n_k_heads) + 31) / 32, 8);
+  const int64_t blocks = resident_blocks((rows + 7) / 8, 8);  // one warp per row
   tg::qk_norm_rope_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "qk_norm_rope launch");
