@@ -19,6 +19,7 @@ import time
 from dataclasses import dataclass
 from typing import List, Optional, Sequence, Union
 
+import numpy as np
 import torch
 
 from .gate import SYNTHETIC_E2E_SEED, LinLogSigGate, load_gate, synthetic_e2e_gate
@@ -45,6 +46,26 @@ def split_state_span(ids: List[int]):
             f"ends={ends}")
     clean = list(ids[:s]) + list(ids[s + 1:e]) + list(ids[e + 1:])
     return clean, s, e - 1
+
+
+def _split_state_span_tensor(ids):
+    """split_state_span for the generate path: one conversion of the ids to an
+    int64 array (a list of Python ints costs ~30 ns per id to convert; the
+    sentinel scan and the cut are vectorized), the clean ids returned as a CPU
+    int64 tensor. Same checks and error as split_state_span."""
+    a = ids.cpu().numpy() if torch.is_tensor(ids) else np.asarray(ids, dtype=np.int64)
+    if a.ndim != 1:
+        raise ValueError(f"ids must be one flat sequence per prompt, got shape {a.shape}")
+    ss = np.flatnonzero(a == STATE_START_ID)
+    ee = np.flatnonzero(a == STATE_END_ID)
+    if len(ss) != 1 or len(ee) != 1 or ss[0] >= ee[0]:
+        raise ValueError(
+            "ids carry no valid state span: expected exactly one STATE_START_ID followed by one "
+            f"STATE_END_ID (produce ids with apply_chat_template(state=...)); found starts={ss.tolist()} "
+            f"ends={ee.tolist()}")
+    s, e = int(ss[0]), int(ee[0])
+    clean = np.concatenate((a[:s], a[s + 1:e], a[e + 1:])).astype(np.int64, copy=False)
+    return torch.from_numpy(clean), s, e - 1
 
 
 def with_state_span(prefix: Sequence[int], state: Sequence[int], suffix: Sequence[int]) -> List[int]:
@@ -87,9 +108,11 @@ class TokenGateModel:
         if max_new_tokens != 1:
             raise NotImplementedError("the B200 build serves the gated prefill (first token); "
                                       "decoding more tokens is outside it: pass max_new_tokens=1")
-        if ids and isinstance(ids[0], int):
+        if torch.is_tensor(ids) or isinstance(ids, np.ndarray):
+            ids = [ids] if ids.ndim == 1 else list(ids)
+        elif len(ids) and isinstance(ids[0], (int, np.integer)):
             ids = [ids]
-        split = [split_state_span(list(seq)) for seq in ids]
+        split = [_split_state_span_tensor(seq) for seq in ids]
         clean = [s[0] for s in split]
         starts = [s[1] for s in split]
         ends = [s[2] for s in split]
