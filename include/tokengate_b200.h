@@ -17,6 +17,7 @@
 #ifndef TOKENGATE_B200_H
 #define TOKENGATE_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -258,6 +259,42 @@ int tg_phase2_tables(const float* scores, int64_t s_sb, int B, const int32_t* st
                      const int32_t* n_kept, int n_alloc, const float* gate_scale,
                      const float* attn_scale, int n_layers, int n_heads, float eps, float gain,
                      float* bias, float* q_scale, void* stream);
+
+/*
+ * f4 — decode attention (the decode side of the gated generation): one
+ * query token per (batch row, head) against the gated KV cache.
+ *
+ * Replaces the decode step's attention of the reference's gated generation,
+ *   generate_batch (tokengate/e2e_gate/decode/gate_decode.py:139-235) with
+ *   FormDecodeState's folded Phase-2 form
+ *   (tokengate/e2e_gate/attn/qwen3_flex_attention.py:374-415, :978-1116):
+ *   out[b,h,:] = sum_j softmax_j( softmax_scale * (q'[b,h,:] . k[b,j,g,:]) + m[b,h,j] ) v[b,j,g,:]
+ *   q' = bf16(q * bf16(q_scale[b,h]))  (q_scale nullable: the per-step
+ *        scaled-softmax query scale gamma * r; no scaling when NULL)
+ *   m  = bias[b,h,j] for j < n_valid[b]; -inf for n_valid[b] <= j < n_prefix
+ *        (pad slots); 0 for n_prefix <= j < n_keys (tokens appended by decode).
+ *
+ * q: (B, Hq, D) bf16 strides (q_sb, q_sh, 1); k, v: (B, cap >= n_keys, Hkv,
+ * D) bf16 strides (k_sb, k_ss, k_sh, 1) — k 16-byte aligned with strides
+ * multiples of 8, v 8-byte aligned with strides multiples of 4. bias: fp32
+ * (B, Hq|1, n_prefix) strides (bias_sb, bias_sh, 1) in score units,
+ * nullable. n_valid: device int32 (B,). out: (B, Hq, D) bf16. Only D == 128
+ * and Hq / Hkv in {1, 2, 4, 8}. workspace: device scratch of
+ * tg_decode_attn_workspace bytes (0 when n_keys <= 256), 16-byte aligned;
+ * calls sharing it must not overlap on the GPU.
+ */
+int tg_decode_attn(const void* q, int64_t q_sb, int64_t q_sh,
+                   const float* q_scale, int64_t qs_sb,
+                   const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                   const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                   const float* bias, int64_t bias_sb, int64_t bias_sh,
+                   const int32_t* n_valid, int n_prefix, int n_keys,
+                   void* out, int64_t o_sb, int64_t o_sh,
+                   void* workspace, size_t workspace_bytes,
+                   int B, int Hq, int Hkv, int D, float softmax_scale, void* stream);
+
+/* Scratch bytes tg_decode_attn needs (0: one key chunk, none). */
+int tg_decode_attn_workspace(int B, int Hq, int n_keys, size_t* bytes);
 
 #ifdef __cplusplus
 }

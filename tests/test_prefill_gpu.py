@@ -182,8 +182,8 @@ def test_generate_api(tiny, cuda):
     assert len(out.token_ids[0]) == 1 and out.prefill_s > 0
     all_keep = tm.generate(ids, None)   # K = all
     assert all_keep.n_kept == [312]
-    with pytest.raises(NotImplementedError):
-        tm.generate(ids, None, max_new_tokens=4)
+    with pytest.raises(ValueError):
+        tm.generate(ids, None, max_new_tokens=0)
     with pytest.raises(ValueError):
         tm.generate(list(range(10)), None)
 

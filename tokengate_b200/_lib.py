@@ -86,6 +86,9 @@ _SIGNATURES = {
     "tg_branch_score": [_P, _I64, _I64, _I32, _P, _I32, _P, _P, _P, _I64, _P],
     "tg_phase2_tables": [_P, _I64, _I32, _P, _P, _P, _I64, _P, _I32, _P, _P, _I32, _I32, _F, _F, _P, _P,
                          _P],
+    "tg_decode_attn": [_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64,
+                       _P, _I32, _I32, _P, _I64, _I64, _P, ctypes.c_size_t, _I32, _I32, _I32, _I32, _F, _P],
+    "tg_decode_attn_workspace": [_I32, _I32, _I32, ctypes.POINTER(ctypes.c_size_t)],
 }
 EXPORTED = tuple(_SIGNATURES)
 

@@ -18,6 +18,7 @@
 #include "gather_rows.cuh"
 #include "layer_glue.cuh"
 #include "e2e_gate.cuh"
+#include "decode_attn.cuh"
 
 // Bit flags set by kernels whose bounded waits gave up (see ptx.cuh).
 __device__ unsigned int g_tg_device_error = 0;
@@ -636,6 +637,97 @@ int tg_phase2_tables(const float* scores, int64_t s_sb, int B, const int32_t* st
     tg::phase2_tables_kernel<<<grid, tg::kTablesThreads, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "phase2_tables launch");
+  }
+  return TG_OK;
+}
+
+namespace {
+int decode_chunks(int n_keys) { return (n_keys + tg::kDecKeys - 1) / tg::kDecKeys; }
+}  // namespace
+
+int tg_decode_attn_workspace(int B, int Hq, int n_keys, size_t* bytes) {
+  if (bytes == nullptr) return fail(TG_ERR_INVALID_ARGUMENT, "bytes must be non-NULL");
+  *bytes = 0;
+  if (B < 1 || Hq < 1 || n_keys < 1)
+    return fail(TG_ERR_INVALID_ARGUMENT, "decode_attn_workspace: B=%d Hq=%d n_keys=%d", B, Hq, n_keys);
+  const int nc = decode_chunks(n_keys);
+  if (nc > 1) *bytes = (size_t)B * Hq * nc * tg::kDecPart * sizeof(float);
+  return TG_OK;
+}
+
+int tg_decode_attn(const void* q, int64_t q_sb, int64_t q_sh, const float* q_scale, int64_t qs_sb,
+                   const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sb,
+                   int64_t v_ss, int64_t v_sh, const float* bias, int64_t bias_sb, int64_t bias_sh,
+                   const int32_t* n_valid, int n_prefix, int n_keys, void* out, int64_t o_sb, int64_t o_sh,
+                   void* workspace, size_t workspace_bytes, int B, int Hq, int Hkv, int D,
+                   float softmax_scale, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || n_valid == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "decode_attn: q, k, v, out and n_valid must be non-NULL");
+  if (B < 1 || B > 65535 || Hq < 1 || Hkv < 1 || n_keys < 1 || n_prefix < 0 || n_prefix > n_keys)
+    return fail(TG_ERR_INVALID_ARGUMENT, "decode_attn: B=%d Hq=%d Hkv=%d n_prefix=%d n_keys=%d", B, Hq, Hkv,
+                n_prefix, n_keys);
+  if (D != 128) return fail(TG_ERR_UNSUPPORTED, "decode_attn: head_dim %d not served (only 128)", D);
+  if (Hq % Hkv != 0)
+    return fail(TG_ERR_INVALID_ARGUMENT, "decode_attn: query heads %d not a multiple of kv heads %d", Hq, Hkv);
+  const int G = Hq / Hkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return fail(TG_ERR_UNSUPPORTED, "decode_attn: %d query heads per kv head (1, 2, 4 or 8 served)", G);
+  if (!(softmax_scale > 0.f)) return fail(TG_ERR_INVALID_ARGUMENT, "decode_attn: softmax_scale must be > 0");
+  if ((reinterpret_cast<uintptr_t>(k) & 15) || ((k_sb | k_ss | k_sh) & 7) ||
+      (reinterpret_cast<uintptr_t>(v) & 7) || ((v_sb | v_ss | v_sh) & 3))
+    return fail(TG_ERR_ALIGNMENT, "decode_attn: k 16-byte aligned with strides multiples of 8 elements, "
+                                  "v 8-byte aligned with strides multiples of 4");
+  const int nc = decode_chunks(n_keys);
+  if (nc > 1) {
+    const size_t need = (size_t)B * Hq * nc * tg::kDecPart * sizeof(float);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(TG_ERR_INVALID_ARGUMENT, "decode_attn: workspace of %zu bytes, %zu needed", workspace_bytes,
+                  need);
+    if (reinterpret_cast<uintptr_t>(workspace) & 15)
+      return fail(TG_ERR_ALIGNMENT, "decode_attn: workspace must be 16-byte aligned");
+  }
+  tg::DecodeParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_sb = q_sb;
+  p.q_sh = q_sh;
+  p.q_scale = q_scale;
+  p.qs_sb = qs_sb;
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.k_sb = k_sb;
+  p.k_ss = k_ss;
+  p.k_sh = k_sh;
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.v_sb = v_sb;
+  p.v_ss = v_ss;
+  p.v_sh = v_sh;
+  p.bias = bias;
+  p.bias_sb = bias_sb;
+  p.bias_sh = bias_sh;
+  p.n_valid = n_valid;
+  p.n_prefix = n_prefix;
+  p.n_keys = n_keys;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.o_sb = o_sb;
+  p.o_sh = o_sh;
+  p.part = static_cast<float*>(workspace);
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.n_chunks = nc;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dim3 grid((unsigned)nc, (unsigned)Hkv, (unsigned)B);
+  switch (G) {
+    case 1: tg::decode_attn_kernel<1><<<grid, tg::kDecThreads, 0, s>>>(p); break;
+    case 2: tg::decode_attn_kernel<2><<<grid, tg::kDecThreads, 0, s>>>(p); break;
+    case 4: tg::decode_attn_kernel<4><<<grid, tg::kDecThreads, 0, s>>>(p); break;
+    default: tg::decode_attn_kernel<8><<<grid, tg::kDecThreads, 0, s>>>(p); break;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "decode_attn launch");
+  if (nc > 1) {
+    tg::decode_combine_kernel<<<dim3((unsigned)Hq, (unsigned)B), tg::kDecD, 0, s>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "decode_attn combine launch");
   }
   return TG_OK;
 }

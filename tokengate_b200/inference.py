@@ -15,6 +15,7 @@ Checkpoint loading covers the linear log-sigmoid gate (a .pt holding
 checkpoints with a scoring branch and LoRA adapters are not served.
 """
 import os
+import re
 import time
 from dataclasses import dataclass
 from typing import List, Optional, Sequence, Union
@@ -68,6 +69,16 @@ def _split_state_span_tensor(ids):
     return torch.from_numpy(clean), s, e - 1
 
 
+_THINK_RE = re.compile(r"<think>.*?</think>", re.DOTALL)
+_THINK_OPEN_RE = re.compile(r"<think>.*", re.DOTALL)
+
+
+def _strip_thinking(text: str) -> str:
+    """Drop <think>...</think> blocks, a trailing unclosed one included, as the
+    reference does with its answers (tokengate/generators.py:382-386)."""
+    return _THINK_OPEN_RE.sub("", _THINK_RE.sub("", text)).strip()
+
+
 def with_state_span(prefix: Sequence[int], state: Sequence[int], suffix: Sequence[int]) -> List[int]:
     """prefix + [STATE_START_ID] + state + [STATE_END_ID] + suffix."""
     return list(prefix) + [STATE_START_ID] + list(state) + [STATE_END_ID] + list(suffix)
@@ -105,9 +116,8 @@ class TokenGateModel:
     def generate(self, ids: Union[List[int], List[List[int]]], tokenizer=None, *,
                  max_new_tokens: int = 1, max_kept_prefill_tokens: Optional[int] = None,
                  streamer=None) -> GenerateOutput:
-        if max_new_tokens != 1:
-            raise NotImplementedError("the B200 build serves the gated prefill (first token); "
-                                      "decoding more tokens is outside it: pass max_new_tokens=1")
+        if max_new_tokens < 1:
+            raise ValueError("max_new_tokens must be positive")
         if torch.is_tensor(ids) or isinstance(ids, np.ndarray):
             ids = [ids] if ids.ndim == 1 else list(ids)
         elif len(ids) and isinstance(ids[0], (int, np.integer)):
@@ -118,6 +128,21 @@ class TokenGateModel:
         ends = [s[2] for s in split]
         k = _NO_PRUNING if max_kept_prefill_tokens is None else max_kept_prefill_tokens
         dev = next(self.model.parameters()).device
+        if max_new_tokens > 1:
+            # gated prefill + greedy decode over the gated KV cache (decode.generate_batch)
+            from .decode import generate_batch
+            eos = getattr(tokenizer, "eos_token_id", None) if tokenizer is not None else None
+            r = generate_batch(self.model, self.gate, clean, starts, ends, self.gate_layer, k,
+                               max_new_tokens, eos_token_id=eos, streamer=streamer)
+            answers = []
+            for toks, n in zip(r.token_ids, r.n_gen):
+                answers.append(_strip_thinking(tokenizer.decode(toks[:n], skip_special_tokens=True))
+                               if tokenizer is not None and n else "")
+            kept_host = r.kept_pos.cpu()
+            kept_pos = [kept_host[b, :n].tolist() for b, n in enumerate(r.n_kepts)]
+            return GenerateOutput(answers=answers, n_kept=list(r.n_kepts),
+                                  n_state=[e - s for s, e in zip(starts, ends)], kept_pos=kept_pos,
+                                  prefill_s=r.prefill_s, decode_s=r.decode_s, token_ids=r.token_ids)
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
         first, _cache, kept, n_kepts, _kc = self.prefill(clean, starts, ends, k)

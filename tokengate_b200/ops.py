@@ -467,3 +467,73 @@ def phase2_tables(scores: torch.Tensor, state_begin: Sequence[int], n_state: Seq
                                       int(Lp), int(H), float(eps), float(gain), bias.data_ptr(),
                                       q_scale.data_ptr(), _stream(scores)))
     return bias, q_scale
+
+
+# ----------------------------------------------------------------- decode attention
+def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_valid: torch.Tensor,
+                     n_prefix: int, n_keys: int, bias: Optional[torch.Tensor] = None,
+                     q_scale: Optional[torch.Tensor] = None,
+                     softmax_scale: Optional[float] = None,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One decode query per (row, head) against a gated KV cache (tg_decode_attn).
+
+    q: (B, Hq, 128) bf16; k, v: (B, cap, Hkv, 128) bf16 caches holding the
+    prefix (kept tokens, or the full Phase-1 cache) in [0, n_prefix) and the
+    decoded tokens in [n_prefix, n_keys); n_valid: (B,) int32 on the device,
+    prefix keys valid per row (the rest are pad slots, masked). bias: fp32
+    broadcastable to (B, Hq, n_prefix) with a contiguous last dim, added to
+    the prefix keys' scores (score units); q_scale: fp32 (B, Hq), the
+    per-step query scale (q <- bf16(q * bf16(q_scale))). Returns (B, Hq, 128) bf16.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(name, t, torch.bfloat16)
+        if t.stride(-1) != 1:
+            raise ValueError(f"{name} must have a contiguous last dim")
+    if q.dim() != 3 or k.dim() != 4 or v.shape != k.shape:
+        raise ValueError(f"shapes: q {tuple(q.shape)} (B, Hq, D), k/v {tuple(k.shape)} (B, cap, Hkv, D)")
+    B, Hq, D = q.shape
+    cap, Hkv = k.shape[1], k.shape[2]
+    if k.shape[0] != B or k.shape[3] != D:
+        raise ValueError(f"shape mismatch: q {tuple(q.shape)} k {tuple(k.shape)}")
+    if not 0 <= n_prefix <= n_keys <= cap:
+        raise ValueError(f"need 0 <= n_prefix ({n_prefix}) <= n_keys ({n_keys}) <= cache capacity ({cap})")
+    _require_cuda("n_valid", n_valid, torch.int32)
+    if n_valid.numel() != B or not n_valid.is_contiguous():
+        raise ValueError("n_valid must be a contiguous (B,) int32 tensor")
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=q.device)
+    bias_ptr, bsb, bsh = None, 0, 0
+    if bias is not None:
+        _require_cuda("bias", bias, torch.float32)
+        bb = bias
+        while bb.dim() < 3:
+            bb = bb.unsqueeze(0)
+        if bb.shape[-1] < n_prefix or bb.stride(-1) != 1 or bb.shape[0] not in (1, B) \
+                or bb.shape[1] not in (1, Hq):
+            raise ValueError(f"bias {tuple(bias.shape)} must broadcast to ({B}, {Hq}, >= {n_prefix}) "
+                             "with a contiguous last dim")
+        bsb = 0 if bb.shape[0] == 1 else bb.stride(0)
+        bsh = 0 if bb.shape[1] == 1 else bb.stride(1)
+        bias_ptr = bb.data_ptr()
+    qs_ptr, qsb = None, 0
+    if q_scale is not None:
+        _require_cuda("q_scale", q_scale, torch.float32)
+        if q_scale.shape != (B, Hq) or q_scale.stride(1) != 1:
+            raise ValueError(f"q_scale must be (B, Hq) = ({B}, {Hq}) with a contiguous last dim")
+        qs_ptr, qsb = q_scale.data_ptr(), q_scale.stride(0)
+    L = _lib.lib()
+    with _device_ctx(q):
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(L.tg_decode_attn_workspace(B, Hq, int(n_keys), ctypes.byref(nbytes)))
+        ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device) if nbytes.value else None
+        _lib.check(L.tg_decode_attn(
+            q.data_ptr(), q.stride(0), q.stride(1), qs_ptr, qsb,
+            k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+            v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
+            bias_ptr, bsb, bsh, n_valid.data_ptr(), int(n_prefix), int(n_keys),
+            out.data_ptr(), out.stride(0), out.stride(1),
+            ws.data_ptr() if ws is not None else None, nbytes.value,
+            B, Hq, Hkv, D, float(softmax_scale), _stream(q)))
+    return out

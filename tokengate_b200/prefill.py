@@ -110,11 +110,19 @@ def _ids_to_device(prompt_ids_list, device) -> torch.Tensor:
 def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequence,
                              article_starts: Sequence[int], article_ends: Sequence[int],
                              gate_layer: int, K: Union[int, Sequence[int]],
-                             prune_below_gate: bool = False, fused: Optional[bool] = None):
+                             prune_below_gate: bool = False, fused: Optional[bool] = None,
+                             decode_state: Optional[dict] = None):
     """fused: run the decoder layers through the fused glue kernels
     (tokengate_b200.layers); None picks it whenever the gate has no learned
     attention scale. False runs the transformers layers with the patched
-    attention module (the reference's structure)."""
+    attention module (the reference's structure).
+
+    decode_state: a dict to receive what the decode side folds from this
+    prefill (the reference reads the same values from the layers' bias /
+    scale attributes, qwen3_flex_attention.py:978-1057): 'bias', one fp32
+    (B, H|1, max_n_kept) Phase-2 key bias per layer above the gate;
+    'gamma', the (L', H) fp32 scaled-softmax gains or None; 'lens'. Fused
+    path only."""
     B = len(prompt_ids_list)
     if B < 1:
         raise ValueError("empty batch")
@@ -282,6 +290,18 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
             hs_pruned = inner.layers[i](hs_pruned, attention_mask=None, position_ids=kept_positions,
                                         past_key_values=cache, use_cache=True, position_embeddings=pe2)
         hs_last = inner.norm(hs_pruned[rows, last_valid])
+
+    if decode_state is not None:
+        if not fused:
+            raise NotImplementedError("decode_state is filled by the fused layer path")
+        if e2e:
+            decode_state["bias"] = [bias_tab[li][:, :, :max_n_kept] for li in range(n_layers - 1 - gate_layer)]
+            decode_state["gamma"] = ew.attn_scale
+        else:
+            row = bias_row[:, :max_n_kept].float().unsqueeze(1)
+            decode_state["bias"] = [row] * (n_layers - 1 - gate_layer)
+            decode_state["gamma"] = None
+        decode_state["lens"] = lens
 
     # ---- head
     first_tokens = model.lm_head(hs_last).argmax(-1, keepdim=True)
