@@ -296,6 +296,31 @@ int tg_decode_attn(const void* q, int64_t q_sb, int64_t q_sh,
 /* Scratch bytes tg_decode_attn needs (0: one key chunk, none). */
 int tg_decode_attn_workspace(int B, int Hq, int n_keys, size_t* bytes);
 
+/*
+ * tg_decode_attn for callers that cannot allocate device memory where they
+ * call it: a host runtime that binds this library over its FFI while owning
+ * the GPU's memory pool itself (so the binding has no allocator to hand a
+ * workspace from), or code on a path where a cudaMalloc is not allowed (it
+ * can synchronize the device, or the memory budget was fixed up front).
+ * Same arguments and results as tg_decode_attn without the workspace: the
+ * key-chunk partials go to a fixed 8 MiB buffer the library keeps on every
+ * GPU that loads it, until the process exits. Nothing is allocated. A
+ * problem needing more than 8 MiB of scratch (B * Hq * ceil(n_keys / 256) *
+ * 520 bytes) is rejected with TG_ERR_INVALID_ARGUMENT. The first call on a
+ * device looks up the buffer's device address (make it before any stream
+ * capture on that device). All calls share the one buffer: calls that
+ * overlap on the GPU race and must be serialized by the caller. No
+ * counterpart in the reference.
+ */
+int tg_decode_attn_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
+                           const float* q_scale, int64_t qs_sb,
+                           const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                           const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                           const float* bias, int64_t bias_sb, int64_t bias_sh,
+                           const int32_t* n_valid, int n_prefix, int n_keys,
+                           void* out, int64_t o_sb, int64_t o_sh,
+                           int B, int Hq, int Hkv, int D, float softmax_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -89,6 +89,8 @@ _SIGNATURES = {
     "tg_decode_attn": [_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64,
                        _P, _I32, _I32, _P, _I64, _I64, _P, ctypes.c_size_t, _I32, _I32, _I32, _I32, _F, _P],
     "tg_decode_attn_workspace": [_I32, _I32, _I32, ctypes.POINTER(ctypes.c_size_t)],
+    "tg_decode_attn_noalloc": [_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64,
+                               _I64, _P, _I32, _I32, _P, _I64, _I64, _I32, _I32, _I32, _I32, _F, _P],
 }
 EXPORTED = tuple(_SIGNATURES)
 

@@ -641,6 +641,12 @@ int tg_phase2_tables(const float* scores, int64_t s_sb, int B, const int32_t* st
   return TG_OK;
 }
 
+// Fixed device scratch for tg_decode_attn_noalloc (each GPU that loads the
+// library holds it until the process exits).
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB
+static __device__ __align__(256) float g_tg_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+float* g_noalloc_ptr[kMaxDevices] = {};
+
 namespace {
 int decode_chunks(int n_keys) { return (n_keys + tg::kDecKeys - 1) / tg::kDecKeys; }
 }  // namespace
@@ -730,6 +736,41 @@ int tg_decode_attn(const void* q, int64_t q_sb, int64_t q_sh, const float* q_sca
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn combine launch");
   }
   return TG_OK;
+}
+
+int tg_decode_attn_noalloc(const void* q, int64_t q_sb, int64_t q_sh, const float* q_scale, int64_t qs_sb,
+                           const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh, const void* v,
+                           int64_t v_sb, int64_t v_ss, int64_t v_sh, const float* bias, int64_t bias_sb,
+                           int64_t bias_sh, const int32_t* n_valid, int n_prefix, int n_keys, void* out,
+                           int64_t o_sb, int64_t o_sh, int B, int Hq, int Hkv, int D, float softmax_scale,
+                           void* stream) {
+  // The key-chunk partials go to the library's fixed per-device buffer
+  // instead of a caller workspace. Its device address is looked up once per
+  // device, with that device current, on the first call made there.
+  size_t need = 0;
+  int st = tg_decode_attn_workspace(B, Hq, n_keys, &need);
+  if (st) return st;
+  if (need > kNoAllocScratchBytes)
+    return fail(TG_ERR_INVALID_ARGUMENT,
+                "decode_attn_noalloc: B=%d Hq=%d n_keys=%d needs %zu bytes of scratch, more than the fixed "
+                "%zu-byte buffer; use tg_decode_attn with a workspace",
+                B, Hq, n_keys, need, kNoAllocScratchBytes);
+  int dev;
+  if ((st = current_device(&dev))) return st;
+  float* scratch;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* ptr = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&ptr, g_tg_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(decode scratch)");
+      g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  return tg_decode_attn(q, q_sb, q_sh, q_scale, qs_sb, k, k_sb, k_ss, k_sh, v, v_sb, v_ss, v_sh, bias, bias_sb,
+                        bias_sh, n_valid, n_prefix, n_keys, out, o_sb, o_sh, scratch, kNoAllocScratchBytes, B,
+                        Hq, Hkv, D, softmax_scale, stream);
 }
 
 }  // extern "C"
