@@ -293,6 +293,21 @@ int tg_decode_attn(const void* q, int64_t q_sb, int64_t q_sh,
                    void* workspace, size_t workspace_bytes,
                    int B, int Hq, int Hkv, int D, float softmax_scale, void* stream);
 
+/* tg_decode_attn with the key count read on the device: n_keys_dev
+ * (device int32, nullable) holds the keys to attend, at most n_keys, which
+ * then sizes the grid and the workspace. Lets one launch, captured once,
+ * serve decode steps whose cache grows by one key per step. Same reference
+ * interface as tg_decode_attn. */
+int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh,
+                      const float* q_scale, int64_t qs_sb,
+                      const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                      const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                      const float* bias, int64_t bias_sb, int64_t bias_sh,
+                      const int32_t* n_valid, int n_prefix, int n_keys, const int32_t* n_keys_dev,
+                      void* out, int64_t o_sb, int64_t o_sh,
+                      void* workspace, size_t workspace_bytes,
+                      int B, int Hq, int Hkv, int D, float softmax_scale, void* stream);
+
 /* Scratch bytes tg_decode_attn needs (0: one key chunk, none). */
 int tg_decode_attn_workspace(int B, int Hq, int n_keys, size_t* bytes);
 

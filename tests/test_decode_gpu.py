@@ -186,3 +186,20 @@ def test_generate_api_decodes_and_stops_at_eos(tiny, cuda):
     n_eos = out.token_ids[0].index(Tok.eos_token_id)
     assert cut.token_ids[0] == out.token_ids[0][:n_eos + 1]
     assert cut.answers[0] == " ".join(map(str, out.token_ids[0][:n_eos]))
+
+
+def test_decode_graph_equals_eager(tiny, cuda):
+    """The decode step replayed as one CUDA graph gives the eager step's logits bit for bit."""
+    g = torch.Generator().manual_seed(23)
+    prompts = [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (280, 300)]
+    gate = LinLogSigGate(512).to(cuda)
+    forced = torch.randint(0, 1000, (2, 7), generator=g)
+    outs = []
+    for use_graph in (False, True):
+        lg = []
+        generate_batch(tiny["model"], gate, prompts, [10, 20], [250, 290], 1, 40, 8, forced_tokens=forced,
+                       logits_out=lg, use_graph=use_graph)
+        outs.append(torch.stack(lg))
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.equal(outs[0], outs[1])

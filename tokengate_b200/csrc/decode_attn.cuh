@@ -42,7 +42,8 @@ struct DecodeParams {
   const float* bias;  // (B, Hq|1, n_prefix) nullable, score units
   int64_t bias_sb, bias_sh;
   const int32_t* n_valid;  // (B,)
-  int n_prefix, n_keys;
+  int n_prefix, n_keys;    // n_keys: the keys, or with n_keys_dev their upper bound (grid size)
+  const int32_t* n_keys_dev;  // nullable: the actual key count, read on the device
   __nv_bfloat16* out;
   int64_t o_sb, o_sh;
   float* part;  // [B][Hq][n_chunks][kDecPart]
@@ -63,6 +64,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(const DecodePa
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int j0 = chunk * kDecKeys;
+  const int n_keys = p.n_keys_dev != nullptr ? min(__ldg(p.n_keys_dev), p.n_keys) : p.n_keys;
 
   // q of the G heads on this kv head, scaled and rounded as the reference does
   for (int idx = t; idx < G * kDecD; idx += kDecThreads) {
@@ -76,14 +78,14 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(const DecodePa
   // ---- scores: thread t takes key j0 + t
   const int j = j0 + t;
   const int nv = __ldg(p.n_valid + b);
-  const bool valid = j < p.n_keys && !(j < p.n_prefix && j >= nv);
+  const bool valid = j < n_keys && !(j < p.n_prefix && j >= nv);
   float sc[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) sc[g] = 0.f;
   if (valid) {
     const uint4* kr = reinterpret_cast<const uint4*>(p.k + (int64_t)b * p.k_sb + (int64_t)j * p.k_ss +
                                                      (int64_t)kvh * p.k_sh);
-#pragma unroll 4
+#pragma unroll
     for (int c = 0; c < kDecD / 8; ++c) {
       const uint4 kv = __ldg(kr + c);
       const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
@@ -155,9 +157,9 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(const DecodePa
   for (int g = 0; g < G; ++g)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
-  const int kend = min(kDecKeys, p.n_keys - j0);
+  const int kend = min(kDecKeys, n_keys - j0);  // <= 0 for a chunk past the keys
   const __nv_bfloat16* vbase = p.v + (int64_t)b * p.v_sb + (int64_t)kvh * p.v_sh + 4 * lane;
-#pragma unroll 4
+#pragma unroll 8
   for (int kk = warp; kk < kend; kk += kDecThreads / 32) {
     const uint2 vv = __ldg(reinterpret_cast<const uint2*>(vbase + (int64_t)(j0 + kk) * p.v_ss));
     const float v0 = __uint_as_float(vv.x << 16), v1 = __uint_as_float(vv.x & 0xFFFF0000u);

@@ -667,6 +667,17 @@ int tg_decode_attn(const void* q, int64_t q_sb, int64_t q_sh, const float* q_sca
                    const int32_t* n_valid, int n_prefix, int n_keys, void* out, int64_t o_sb, int64_t o_sh,
                    void* workspace, size_t workspace_bytes, int B, int Hq, int Hkv, int D,
                    float softmax_scale, void* stream) {
+  return tg_decode_attn_ex(q, q_sb, q_sh, q_scale, qs_sb, k, k_sb, k_ss, k_sh, v, v_sb, v_ss, v_sh, bias,
+                           bias_sb, bias_sh, n_valid, n_prefix, n_keys, nullptr, out, o_sb, o_sh, workspace,
+                           workspace_bytes, B, Hq, Hkv, D, softmax_scale, stream);
+}
+
+int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh, const float* q_scale, int64_t qs_sb,
+                      const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sb,
+                      int64_t v_ss, int64_t v_sh, const float* bias, int64_t bias_sb, int64_t bias_sh,
+                      const int32_t* n_valid, int n_prefix, int n_keys, const int32_t* n_keys_dev, void* out,
+                      int64_t o_sb, int64_t o_sh, void* workspace, size_t workspace_bytes, int B, int Hq,
+                      int Hkv, int D, float softmax_scale, void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || n_valid == nullptr)
     return fail(TG_ERR_INVALID_ARGUMENT, "decode_attn: q, k, v, out and n_valid must be non-NULL");
   if (B < 1 || B > 65535 || Hq < 1 || Hkv < 1 || n_keys < 1 || n_prefix < 0 || n_prefix > n_keys)
@@ -712,6 +723,7 @@ int tg_decode_attn(const void* q, int64_t q_sb, int64_t q_sh, const float* q_sca
   p.n_valid = n_valid;
   p.n_prefix = n_prefix;
   p.n_keys = n_keys;
+  p.n_keys_dev = n_keys_dev;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.o_sb = o_sb;
   p.o_sh = o_sh;

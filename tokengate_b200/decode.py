@@ -80,13 +80,16 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
                    max_new_tokens: int, *, eos_token_id: Optional[int] = None,
                    phase2_form: bool = True, prune_below_gate: bool = False,
                    streamer=None, forced_tokens: Optional[torch.Tensor] = None,
-                   logits_out: Optional[list] = None) -> GateGenerateResult:
+                   logits_out: Optional[list] = None, use_graph: bool = True) -> GateGenerateResult:
     """Gated prefill + greedy decode of up to max_new_tokens tokens per row.
 
     forced_tokens: (B, max_new_tokens - 1) ids fed to the decode steps in
     place of the previous step's argmax (teacher forcing, to score a given
     continuation);
-    logits_out: a list that receives each decode step's (B, vocab) fp32 logits."""
+    logits_out: a list that receives each decode step's (B, vocab) fp32 logits;
+    use_graph: replay the decode step as one CUDA graph after the first
+    (eager) step — the state a step reads (token, position, append slot, key
+    count) lives in device buffers the step itself advances."""
     if max_new_tokens < 1:
         raise ValueError("max_new_tokens must be positive")
     device = next(model.parameters()).device
@@ -127,53 +130,86 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
             r = (torch.log(m) / torch.log(pp)).clamp(max=1.0)
             gam = st["gamma"].float()                                                   # (L', H)
             qs_all = (gam[None, :, None, :] * r[:, None, :, None]).contiguous()        # (steps, L', B, H)
-        eos_seen = torch.zeros(B, dtype=torch.bool, device=device)
-        cur = first
         lw0 = fw[0]
         nq, nkv, D = lw0.n_q, lw0.n_kv, lw0.head_dim
-        for step in range(max_new_tokens - 1):
-            if eos_token_id is not None:
-                eos_seen |= cur[:, 0] == eos_token_id
-                if bool(eos_seen.all()):
-                    break
-            if forced_tokens is not None:
-                cur = forced_tokens[:, step:step + 1].to(device=device, dtype=cur.dtype)
+        # step state on the device, so that one captured step serves every
+        # step: the token, its position, each cache's append slot and key count
+        cur = first.clone()
+        pos = next_pos.view(B, 1).clone()
+        wb, w2 = dc.width[0], dc.width[n_layers - 1]
+        slot_b = torch.tensor([wb], dtype=torch.int64, device=device)
+        slot_2 = torch.tensor([w2], dtype=torch.int64, device=device)
+        nk_b = torch.tensor([wb + 1], dtype=torch.int32, device=device)
+        nk_2 = torch.tensor([w2 + 1], dtype=torch.int32, device=device)
+        qs_cur = torch.empty_like(qs_all[0]) if qs_all is not None else None
+        lg_buf = torch.empty((B, model.lm_head.weight.shape[0]), dtype=torch.float32, device=device)
+        extra = max_new_tokens - 1
+
+        def step_body():
             h = inner.embed_tokens(cur)                                               # (B, 1, H)
-            pos = next_pos.view(B, 1)
             cos, sin = inner.rotary_emb(h, pos)
             delta = None
             for i in range(n_layers):
                 lw = fw[i]
+                below = i <= gate_layer
                 h, x = ops.add_rmsnorm(h, delta, lw.in_w, lw.eps, h_out=h if delta is not None else None)
                 qkv = F.linear(x, lw.wqkv).view(B, 1, nq + 2 * nkv, D)
                 q = qkv[:, :, :nq]
                 k = qkv[:, :, nq:nq + nkv]
                 v = qkv[:, :, nq + nkv:]
                 ops.qk_norm_rope(q, k, lw.q_norm_w, lw.k_norm_w, cos, sin, lw.qk_eps)
+                slot = slot_b if below else slot_2
+                dc.k[i].index_copy_(1, slot, k)
+                dc.v[i].index_copy_(1, slot, v)
                 W = dc.width[i]
-                slot = W + step
-                dc.k[i][:, slot].copy_(k[:, 0])
-                dc.v[i][:, slot].copy_(v[:, 0])
-                if i > gate_layer:
-                    li = i - gate_layer - 1
-                    a = ops.decode_attention(q[:, 0], dc.k[i], dc.v[i], n_kept_dev, W, slot + 1,
-                                             bias=bias[li],
-                                             q_scale=qs_all[step, li] if qs_all is not None else None)
+                if below:
+                    a = ops.decode_attention(q[:, 0], dc.k[i], dc.v[i], valid_below, W, W + extra,
+                                             n_keys_dev=nk_b)
                 else:
-                    a = ops.decode_attention(q[:, 0], dc.k[i], dc.v[i], valid_below, W, slot + 1)
+                    li = i - gate_layer - 1
+                    a = ops.decode_attention(q[:, 0], dc.k[i], dc.v[i], n_kept_dev, W, W + extra,
+                                             bias=bias[li], q_scale=qs_cur[li] if qs_cur is not None else None,
+                                             n_keys_dev=nk_2)
                 o = F.linear(a.view(B, 1, nq * D), lw.wo)
                 h, x2 = ops.add_rmsnorm(h, o, lw.post_w, lw.eps, h_out=h)
                 delta = layer_mlp(lw, x2)
             _, hn = ops.add_rmsnorm(h, delta, inner.norm.weight, float(inner.norm.variance_epsilon))
             lg = model.lm_head(hn)[:, -1]
+            lg_buf.copy_(lg)
+            cur.copy_(lg.argmax(-1, keepdim=True))
+            pos.add_(1)
+            for t_ in (slot_b, slot_2, nk_b, nk_2):
+                t_.add_(1)
+
+        graph = None
+        eos_seen = torch.zeros(B, dtype=torch.bool, device=device)
+        for step in range(extra):
+            if eos_token_id is not None:
+                eos_seen |= cur[:, 0] == eos_token_id
+                if bool(eos_seen.all()):
+                    break
+            if forced_tokens is not None:
+                cur.copy_(forced_tokens[:, step:step + 1].to(device=device, dtype=cur.dtype))
+            if qs_cur is not None:
+                qs_cur.copy_(qs_all[step])
+            if graph is None and use_graph and step > 0:
+                # the first step ran eagerly (library handles, kernel attributes);
+                # capture the same body once, replay it for the rest
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    step_body()
+            if graph is not None:
+                graph.replay()
+            else:
+                step_body()
             if logits_out is not None:
-                logits_out.append(lg.float())
-            cur = lg.argmax(-1, keepdim=True)
+                logits_out.append(lg_buf.clone())
+            nxt = cur.clone()
             if streamer is not None:
-                streamer.put(cur.detach().cpu())
-            gen.append(cur)
-            next_pos = next_pos + 1
+                streamer.put(nxt.detach().cpu())
+            gen.append(nxt)
             steps += 1
+        del graph
     _sync(device)
     decode_s = time.perf_counter() - t1
     if streamer is not None:

@@ -6,6 +6,8 @@
     python -m tokengate_b200.microbench gather [--k 2000] [--batch 1] [--iters 20]
     python -m tokengate_b200.microbench branch [--seq 32768] [--inter 6144] [--batch 1]
     python -m tokengate_b200.microbench tables [--k 2000] [--layers 26] [--hq 16] [--batch 1]
+    python -m tokengate_b200.microbench decode [--seq 2768] [--batch 1] [--hq 16] [--hkv 8] [--no-bias]
+    python -m tokengate_b200.microbench generate [--seq 32768] [--k 2000] [--batch 1] [--new 64] [--gate linear|e2e]
 
 Prints one JSON line per run with the CUDA-event time per launch and the
 algorithmic FLOPs or bytes of one launch (attention: 4*B*Hq*D*S(S+1)/2;
@@ -13,7 +15,11 @@ score: the bf16 state rows + w + fp32 scores; topk: scores read + keep/bias
 written; gather: hidden rows + 4 below-gate K/V tensors read and written;
 branch: the bf16 [gate | up] state rows + w + fp32 scores; tables: the raw
 scores and kept positions read once + both fp32 (L', B, H, n_alloc) tables
-written).
+written; decode: the K and V rows of the n_keys cached tokens + q, bias
+row and output, timed as 20 launches in one CUDA graph so the host launch
+path is not what is measured). generate: the gated generation of the
+BASELINE config-3 model (Qwen3-1.7B shape, random init) — prefill seconds
+and decode milliseconds per token.
 """
 import argparse
 import json
@@ -36,9 +42,35 @@ def _time(fn, iters, warmup=3):
     return e0.elapsed_time(e1) / iters
 
 
+def _graph_time(fn, n, reps, warmup=3):
+    """ms per call of fn, with n calls captured in one CUDA graph and replayed reps times."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(n):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / (reps * n)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=("attn", "score", "topk", "gather", "branch", "tables"))
+    ap.add_argument("kernel", choices=("attn", "score", "topk", "gather", "branch", "tables", "decode",
+                                       "generate"))
+    ap.add_argument("--new", type=int, default=64)
+    ap.add_argument("--gate", default="linear", choices=("linear", "e2e"))
     ap.add_argument("--inter", type=int, default=6144)
     ap.add_argument("--layers", type=int, default=26)
     ap.add_argument("--seq", type=int, default=32768)
@@ -54,7 +86,37 @@ def main(argv=None):
     g = torch.Generator(device=dev).manual_seed(0)
     B, S = a.batch, a.seq
     res = dict(kernel=a.kernel, batch=B)
-    if a.kernel == "attn":
+    if a.kernel == "decode":
+        cap = S + 8
+        q = torch.randn(B, a.hq, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        k = torch.randn(B, cap, a.hkv, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        v = torch.randn(B, cap, a.hkv, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        bias = None if a.no_bias else torch.randn(B, a.hq, S, device=dev, generator=g)
+        qs = None if a.no_bias else torch.rand(B, a.hq, device=dev, generator=g) + 0.5
+        nv = torch.full((B,), S, dtype=torch.int32, device=dev)
+        out = torch.empty(B, a.hq, 128, device=dev, dtype=torch.bfloat16)
+        fn = lambda: ops.decode_attention(q, k, v, nv, S, S + 1, bias=bias, q_scale=qs, out=out)
+        ms = _graph_time(fn, 20, a.iters)
+        byts = B * ((S + 1) * a.hkv * 128 * 2 * 2 + a.hq * 128 * 4 + (0 if a.no_bias else a.hq * S * 4))
+        res.update(seq=S, hq=a.hq, hkv=a.hkv, bias=not a.no_bias, ms=ms, us=ms * 1e3, mbytes=byts / 1e6,
+                   gbs=byts / ms / 1e6)
+    elif a.kernel == "generate":
+        from .decode import generate_batch
+        from .inference import load_model
+        tm = load_model(base_model="qwen3-1.7b", gate_layer=1, gate_attn="b200", device=dev, seed=0,
+                        gate="e2e" if a.gate == "e2e" else None)
+        vocab = tm.model.config.vocab_size
+        gh = torch.Generator().manual_seed(1000)
+        prompts = [torch.randint(0, vocab, (S,), generator=gh) for _ in range(B)]
+        st0, st1 = 512, S - 256
+        run = lambda n: generate_batch(tm.model, tm.gate, prompts, [st0] * B, [st1] * B, 1, a.k, n)
+        run(4)
+        run(a.new)
+        r = run(a.new)
+        res.update(seq=S, k=a.k, gate=a.gate, new=a.new, prefill_ms=r.prefill_s * 1e3,
+                   decode_ms_per_token=r.decode_s * 1e3 / max(r.steps, 1),
+                   decode_tokens_per_s=B * r.steps / r.decode_s if r.steps else None)
+    elif a.kernel == "attn":
         q = torch.randn(B, S, a.hq, 128, device=dev, dtype=torch.bfloat16, generator=g)
         k = torch.randn(B, S, a.hkv, 128, device=dev, dtype=torch.bfloat16, generator=g)
         v = torch.randn(B, S, a.hkv, 128, device=dev, dtype=torch.bfloat16, generator=g)

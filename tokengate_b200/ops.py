@@ -474,7 +474,8 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_valid:
                      n_prefix: int, n_keys: int, bias: Optional[torch.Tensor] = None,
                      q_scale: Optional[torch.Tensor] = None,
                      softmax_scale: Optional[float] = None,
-                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     out: Optional[torch.Tensor] = None,
+                     n_keys_dev: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One decode query per (row, head) against a gated KV cache (tg_decode_attn).
 
     q: (B, Hq, 128) bf16; k, v: (B, cap, Hkv, 128) bf16 caches holding the
@@ -483,7 +484,10 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_valid:
     prefix keys valid per row (the rest are pad slots, masked). bias: fp32
     broadcastable to (B, Hq, n_prefix) with a contiguous last dim, added to
     the prefix keys' scores (score units); q_scale: fp32 (B, Hq), the
-    per-step query scale (q <- bf16(q * bf16(q_scale))). Returns (B, Hq, 128) bf16.
+    per-step query scale (q <- bf16(q * bf16(q_scale))). n_keys_dev: an int32
+    (1,) device tensor holding the keys to attend (at most n_keys, which then
+    only bounds the launch): the form a captured CUDA graph replays while the
+    cache grows (tg_decode_attn_ex). Returns (B, Hq, 128) bf16.
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
         _require_cuda(name, t, torch.bfloat16)
@@ -528,11 +532,14 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_valid:
         nbytes = ctypes.c_size_t(0)
         _lib.check(L.tg_decode_attn_workspace(B, Hq, int(n_keys), ctypes.byref(nbytes)))
         ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device) if nbytes.value else None
-        _lib.check(L.tg_decode_attn(
+        if n_keys_dev is not None:
+            _require_cuda("n_keys_dev", n_keys_dev, torch.int32)
+        _lib.check(L.tg_decode_attn_ex(
             q.data_ptr(), q.stride(0), q.stride(1), qs_ptr, qsb,
             k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
             v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
             bias_ptr, bsb, bsh, n_valid.data_ptr(), int(n_prefix), int(n_keys),
+            n_keys_dev.data_ptr() if n_keys_dev is not None else None,
             out.data_ptr(), out.stride(0), out.stride(1),
             ws.data_ptr() if ws is not None else None, nbytes.value,
             B, Hq, Hkv, D, float(softmax_scale), _stream(q)))
