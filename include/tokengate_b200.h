@@ -201,6 +201,19 @@ int tg_qk_norm_rope(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k,
                     const void* cos, const void* sin, int64_t cs_sb, int64_t cs_ss, int head_dim,
                     float eps, void* stream);
 
+/* tg_qk_norm_rope for one decode token per row (seq == 1) that also
+ * appends it to the layer's caches: the finished k heads and the v heads
+ * (rows x n_k_heads x 128, row stride ld_v) are written to slot *slot_dev
+ * (device int64) of k_cache / v_cache, (B = rows, cap, n_k_heads, 128) with
+ * batch stride cache_sb and slot stride cache_ss. One launch instead of
+ * three per layer and decode step (the reference's DynamicCache.update in
+ * the decode layers, tokengate/e2e_gate/attn/qwen3_flex_attention.py:395-398). */
+int tg_qk_norm_rope_append(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k, int n_k_heads,
+                           const void* v, int64_t ld_v, int64_t rows, const void* q_norm_w,
+                           const void* k_norm_w, const void* cos, const void* sin, int64_t cs_sb,
+                           int64_t cs_ss, int head_dim, float eps, void* k_cache, void* v_cache,
+                           int64_t cache_sb, int64_t cache_ss, const int64_t* slot_dev, void* stream);
+
 /* out[r, :] = bf16(bf16(silu(g)) * u) for a fused row [g (inter) | u (inter)]. */
 int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_t rows, int64_t inter,
                 void* stream);

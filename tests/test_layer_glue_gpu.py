@@ -85,6 +85,32 @@ def test_qk_norm_rope(cuda):
     assert torch.equal(q2, got[:, :, :nq]) and torch.equal(k2, got[:, :, nq:nq + nkv])
 
 
+def test_qk_norm_rope_append(cuda):
+    """The decode form: one token per row, q/k normalised and rotated as by
+    qk_norm_rope, and the finished k plus the v rows written to the caches'
+    slot (read from the device)."""
+    B, nq, nkv, D, cap = 3, 32, 8, 128, 50
+    g = torch.Generator(device=cuda).manual_seed(3)
+    qkv = torch.randn(B, 1, nq + 2 * nkv, D, device=cuda, generator=g).to(torch.bfloat16)
+    qw = (1 + 0.2 * torch.randn(D, device=cuda, generator=g)).to(torch.bfloat16)
+    kw = (1 + 0.2 * torch.randn(D, device=cuda, generator=g)).to(torch.bfloat16)
+    cos = torch.randn(B, 1, D, device=cuda, generator=g).to(torch.bfloat16)
+    sin = torch.randn(B, 1, D, device=cuda, generator=g).to(torch.bfloat16)
+    ref = qkv.clone()
+    ops.qk_norm_rope(ref[:, :, :nq], ref[:, :, nq:nq + nkv], qw, kw, cos, sin, 1e-6)
+    kc = torch.randn(B, cap, nkv, D, device=cuda, generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, cap, nkv, D, device=cuda, generator=g).to(torch.bfloat16)
+    kc0, vc0 = kc.clone(), vc.clone()
+    slot = torch.tensor([37], dtype=torch.int64, device=cuda)
+    got = qkv.clone()
+    ops.qk_norm_rope_append(got[:, :, :nq], got[:, :, nq:nq + nkv], got[:, :, nq + nkv:], qw, kw, cos, sin,
+                            1e-6, kc, vc, slot)
+    assert torch.equal(got, ref)
+    assert torch.equal(kc[:, 37], ref[:, 0, nq:nq + nkv]) and torch.equal(vc[:, 37], qkv[:, 0, nq + nkv:])
+    others = [s for s in range(cap) if s != 37]
+    assert torch.equal(kc[:, others], kc0[:, others]) and torch.equal(vc[:, others], vc0[:, others])
+
+
 def test_silu_mul(cuda):
     g = torch.Generator(device=cuda).manual_seed(2)
     gu = (torch.randn(5, 77, 2 * 6144, device=cuda, generator=g) * 3).to(torch.bfloat16)

@@ -116,6 +116,15 @@ struct QkRopeParams {
   const __nv_bfloat16* sin;
   int64_t cs_sb, cs_ss;        // cos/sin batch and row strides (elements)
   float eps;
+  // decode append (k_cache nullable; one token per batch row, seq == 1): the
+  // finished k heads and the v heads are also written to slot *slot_dev of
+  // the (B, cap, n_k, 128) caches (batch stride kc_sb, slot stride kc_ss)
+  const __nv_bfloat16* v;      // (rows, n_k, 128), row stride ld_v
+  int64_t ld_v;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int64_t kc_sb, kc_ss;
+  const int64_t* slot_dev;
 };
 
 // One warp per row: the row's cos / sin and the two norm gains are loaded
@@ -211,6 +220,21 @@ __global__ void __launch_bounds__(256, 3) qk_norm_rope_kernel(const QkRopeParams
     }
     __nv_bfloat16* qrow = p.q + row * p.ld_q;
     __nv_bfloat16* krow = p.k + row * p.ld_k;
+    __nv_bfloat16* kcrow = nullptr;
+    __nv_bfloat16* vcrow = nullptr;
+    if (p.k_cache != nullptr) {
+      const int64_t slot = __ldg(p.slot_dev);
+      kcrow = p.k_cache + row * p.kc_sb + slot * p.kc_ss;
+      vcrow = p.v_cache + row * p.kc_sb + slot * p.kc_ss;
+      // v heads: straight copy into the cache
+      const uint2* vrow = reinterpret_cast<const uint2*>(p.v + row * p.ld_v);
+      for (int hd = half; hd < p.n_k; hd += 2) {
+        const uint2 a = vrow[hd * 32 + hl], c = vrow[hd * 32 + 16 + hl];
+        uint2* dst = reinterpret_cast<uint2*>(vcrow + (int64_t)hd * 128);
+        dst[hl] = a;
+        dst[16 + hl] = c;
+      }
+    }
     // the head loop is uniform across the warp (the shuffles need every lane)
     for (int h0 = 0; h0 < heads; h0 += 2 * kQkBatch) {
       uint2 xl[kQkBatch], xh[kQkBatch];
@@ -244,6 +268,11 @@ __global__ void __launch_bounds__(256, 3) qk_norm_rope_kernel(const QkRopeParams
                                                     : krow + (int64_t)(hd - p.n_q) * 128);
           xp[hl] = ol;
           xp[16 + hl] = oh;
+          if (!is_q && kcrow != nullptr) {
+            uint2* cp = reinterpret_cast<uint2*>(kcrow + (int64_t)(hd - p.n_q) * 128);
+            cp[hl] = ol;
+            cp[16 + hl] = oh;
+          }
         }
       }
     }

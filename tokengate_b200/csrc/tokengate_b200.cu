@@ -467,10 +467,21 @@ int tg_add_rmsnorm(const void* h_in, int64_t ld_h_in, const void* delta, int64_t
   return TG_OK;
 }
 
-int tg_qk_norm_rope(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k, int n_k_heads,
-                    int64_t rows, int seq, const void* q_norm_w, const void* k_norm_w,
-                    const void* cos, const void* sin, int64_t cs_sb, int64_t cs_ss, int head_dim,
-                    float eps, void* stream) {
+namespace {
+struct AppendArgs {
+  const void* v;
+  int64_t ld_v;
+  void* k_cache;
+  void* v_cache;
+  int64_t kc_sb, kc_ss;
+  const int64_t* slot_dev;
+};
+}  // namespace
+
+static int qk_norm_rope_impl(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k, int n_k_heads,
+                             int64_t rows, int seq, const void* q_norm_w, const void* k_norm_w,
+                             const void* cos, const void* sin, int64_t cs_sb, int64_t cs_ss, int head_dim,
+                             float eps, const AppendArgs* append, void* stream) {
   if (q == nullptr || k == nullptr || q_norm_w == nullptr || k_norm_w == nullptr || cos == nullptr ||
       sin == nullptr)
     return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope: NULL argument");
@@ -502,11 +513,50 @@ int tg_qk_norm_rope(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k,
   p.cs_sb = cs_sb;
   p.cs_ss = cs_ss;
   p.eps = eps;
+  p.v = nullptr;
+  p.ld_v = 0;
+  p.k_cache = p.v_cache = nullptr;
+  p.kc_sb = p.kc_ss = 0;
+  p.slot_dev = nullptr;
+  if (append != nullptr) {
+    p.v = static_cast<const __nv_bfloat16*>(append->v);
+    p.ld_v = append->ld_v;
+    p.k_cache = static_cast<__nv_bfloat16*>(append->k_cache);
+    p.v_cache = static_cast<__nv_bfloat16*>(append->v_cache);
+    p.kc_sb = append->kc_sb;
+    p.kc_ss = append->kc_ss;
+    p.slot_dev = append->slot_dev;
+  }
   const int64_t blocks = resident_blocks((rows + 7) / 8, 8);  // one warp per row
   tg::qk_norm_rope_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "qk_norm_rope launch");
   return TG_OK;
+}
+
+int tg_qk_norm_rope(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k, int n_k_heads,
+                    int64_t rows, int seq, const void* q_norm_w, const void* k_norm_w,
+                    const void* cos, const void* sin, int64_t cs_sb, int64_t cs_ss, int head_dim,
+                    float eps, void* stream) {
+  return qk_norm_rope_impl(q, ld_q, n_q_heads, k, ld_k, n_k_heads, rows, seq, q_norm_w, k_norm_w, cos, sin,
+                           cs_sb, cs_ss, head_dim, eps, nullptr, stream);
+}
+
+int tg_qk_norm_rope_append(void* q, int64_t ld_q, int n_q_heads, void* k, int64_t ld_k, int n_k_heads,
+                           const void* v, int64_t ld_v, int64_t rows, const void* q_norm_w,
+                           const void* k_norm_w, const void* cos, const void* sin, int64_t cs_sb,
+                           int64_t cs_ss, int head_dim, float eps, void* k_cache, void* v_cache,
+                           int64_t cache_sb, int64_t cache_ss, const int64_t* slot_dev, void* stream) {
+  if (v == nullptr || k_cache == nullptr || v_cache == nullptr || slot_dev == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope_append: v, caches and slot must be non-NULL");
+  if (ld_v < (int64_t)n_k_heads * 128 || cache_ss < (int64_t)n_k_heads * 128)
+    return fail(TG_ERR_INVALID_ARGUMENT, "qk_norm_rope_append: v row / cache slot strides shorter than the heads");
+  if (((reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(k_cache) |
+        reinterpret_cast<uintptr_t>(v_cache)) & 15) || ((ld_v | cache_sb | cache_ss) & 7))
+    return fail(TG_ERR_ALIGNMENT, "qk_norm_rope_append: v and caches 16-byte aligned, strides multiples of 8");
+  AppendArgs ap{v, ld_v, k_cache, v_cache, cache_sb, cache_ss, slot_dev};
+  return qk_norm_rope_impl(q, ld_q, n_q_heads, k, ld_k, n_k_heads, rows, 1, q_norm_w, k_norm_w, cos, sin,
+                           cs_sb, cs_ss, head_dim, eps, &ap, stream);
 }
 
 int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_t rows, int64_t inter,

@@ -157,10 +157,8 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
                 q = qkv[:, :, :nq]
                 k = qkv[:, :, nq:nq + nkv]
                 v = qkv[:, :, nq + nkv:]
-                ops.qk_norm_rope(q, k, lw.q_norm_w, lw.k_norm_w, cos, sin, lw.qk_eps)
-                slot = slot_b if below else slot_2
-                dc.k[i].index_copy_(1, slot, k)
-                dc.v[i].index_copy_(1, slot, v)
+                ops.qk_norm_rope_append(q, k, v, lw.q_norm_w, lw.k_norm_w, cos, sin, lw.qk_eps,
+                                        dc.k[i], dc.v[i], slot_b if below else slot_2)
                 W = dc.width[i]
                 if below:
                     a = ops.decode_attention(q[:, 0], dc.k[i], dc.v[i], valid_below, W, W + extra,

@@ -365,6 +365,44 @@ def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_norm_w: torch.Tensor, k_nor
                                      float(eps), _stream(q)))
 
 
+def qk_norm_rope_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm_w: torch.Tensor,
+                        k_norm_w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, eps: float,
+                        k_cache: torch.Tensor, v_cache: torch.Tensor, slot: torch.Tensor) -> None:
+    """qk_norm_rope for one decode token per row, appending it to the caches.
+
+    q (B, 1, Hq, 128), k / v (B, 1, Hkv, 128) with contiguous heads; cos/sin
+    (B, 1, 128); k_cache / v_cache (B, cap, Hkv, 128) contiguous; slot: an
+    int64 (1,) device tensor, the cache slot the token goes to. q and k are
+    normalised and rotated in place; the finished k and the v rows are also
+    written to the caches (tg_qk_norm_rope_append)."""
+    for nm, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(nm, t, torch.bfloat16)
+        if t.dim() != 4 or t.shape[1] != 1 or t.shape[-1] != 128 or t.stride(-1) != 1 or t.stride(-2) != 128:
+            raise ValueError(f"{nm} must be (B, 1, heads, 128) with contiguous heads")
+    B = q.shape[0]
+    if k.shape != v.shape or k.shape[0] != B:
+        raise ValueError("k and v must be (B, 1, Hkv, 128)")
+    for nm, t in (("k_cache", k_cache), ("v_cache", v_cache)):
+        _require_cuda(nm, t, torch.bfloat16)
+        if t.dim() != 4 or t.shape[0] != B or t.shape[2:] != k.shape[2:] or not t.is_contiguous():
+            raise ValueError(f"{nm} must be a contiguous (B, cap, Hkv, 128) tensor")
+    if k_cache.shape != v_cache.shape:
+        raise ValueError("k_cache and v_cache must have one shape")
+    _require_cuda("slot", slot, torch.int64)
+    for nm, t in (("cos", cos), ("sin", sin)):
+        _require_cuda(nm, t, torch.bfloat16)
+        if t.shape != (B, 1, 128) or t.stride(-1) != 1:
+            raise ValueError(f"{nm} must be (B, 1, 128) with a contiguous last dim")
+    L = _lib.lib()
+    with _device_ctx(q):
+        _lib.check(L.tg_qk_norm_rope_append(
+            q.data_ptr(), q.stride(0), q.shape[2], k.data_ptr(), k.stride(0), k.shape[2],
+            v.data_ptr(), v.stride(0), B, q_norm_w.data_ptr(), k_norm_w.data_ptr(),
+            cos.data_ptr(), sin.data_ptr(), cos.stride(0), cos.stride(1), 128, float(eps),
+            k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), slot.data_ptr(),
+            _stream(q)))
+
+
 def silu_mul(gu: torch.Tensor) -> torch.Tensor:
     """gu (..., 2*I) = [gate | up] -> bf16(bf16(silu(gate)) * up) (..., I)."""
     _require_cuda("gu", gu, torch.bfloat16)
