@@ -288,12 +288,12 @@ int tg_phase2_tables(const float* scores, int64_t s_sb, int B, const int32_t* st
  *        (pad slots); 0 for n_prefix <= j < n_keys (tokens appended by decode).
  *
  * q: (B, Hq, D) bf16 strides (q_sb, q_sh, 1); k, v: (B, cap >= n_keys, Hkv,
- * D) bf16 strides (k_sb, k_ss, k_sh, 1) — k 16-byte aligned with strides
- * multiples of 8, v 8-byte aligned with strides multiples of 4. bias: fp32
+ * D) bf16 strides (k_sb, k_ss, k_sh, 1) — 16-byte aligned with strides
+ * multiples of 8. bias: fp32
  * (B, Hq|1, n_prefix) strides (bias_sb, bias_sh, 1) in score units,
  * nullable. n_valid: device int32 (B,). out: (B, Hq, D) bf16. Only D == 128
  * and Hq / Hkv in {1, 2, 4, 8}. workspace: device scratch of
- * tg_decode_attn_workspace bytes (0 when n_keys <= 256), 16-byte aligned;
+ * tg_decode_attn_workspace bytes (0 when n_keys <= 128), 16-byte aligned;
  * calls sharing it must not overlap on the GPU.
  */
 int tg_decode_attn(const void* q, int64_t q_sb, int64_t q_sh,
@@ -333,8 +333,8 @@ int tg_decode_attn_workspace(int B, int Hq, int n_keys, size_t* bytes);
  * Same arguments and results as tg_decode_attn without the workspace: the
  * key-chunk partials go to a fixed 8 MiB buffer the library keeps on every
  * GPU that loads it, until the process exits. Nothing is allocated. A
- * problem needing more than 8 MiB of scratch (B * Hq * ceil(n_keys / 256) *
- * 520 bytes) is rejected with TG_ERR_INVALID_ARGUMENT. The first call on a
+ * problem needing more than 8 MiB of scratch (B * Hq * ceil(n_keys / 128) *
+ * 528 bytes) is rejected with TG_ERR_INVALID_ARGUMENT. The first call on a
  * device looks up the buffer's device address (make it before any stream
  * capture on that device). All calls share the one buffer: calls that
  * overlap on the GPU race and must be serialized by the caller. No

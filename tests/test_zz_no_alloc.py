@@ -57,7 +57,7 @@ def test_noalloc_decode_matches_workspace_entry(cuda):
 
 
 def test_noalloc_decode_rejects_oversized(cuda):
-    # 64 rows x 32 heads x 40 key chunks x 520 B = 42.6 MB of partials > 8 MiB:
+    # 64 rows x 32 heads x 80 key chunks x 528 B = 86.5 MB of partials > 8 MiB:
     # refused from the sizes alone, before any operand is read (so small
     # stand-in tensors do)
     q = torch.zeros(64, 32, 128, dtype=torch.bfloat16, device=cuda)

@@ -255,6 +255,14 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
 
+// 16-byte asynchronous global -> shared copy (L2 only), with its group
+// commit / wait.
+__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // 16-byte read-only global load that does not allocate in L1 (streamed data).
 __device__ __forceinline__ uint4 ld_nc_v4(const uint4* ptr) {
   uint4 v;

@@ -43,6 +43,7 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 unsigned int* g_err_ptr[kMaxDevices] = {};
 bool g_attn_attr_set[kMaxDevices] = {};
+bool g_dec_attr_set[kMaxDevices] = {};
 
 int sm_count() {
   int dev = 0, sms = 148;
@@ -740,10 +741,9 @@ int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh, const float* q_
   if (G != 1 && G != 2 && G != 4 && G != 8)
     return fail(TG_ERR_UNSUPPORTED, "decode_attn: %d query heads per kv head (1, 2, 4 or 8 served)", G);
   if (!(softmax_scale > 0.f)) return fail(TG_ERR_INVALID_ARGUMENT, "decode_attn: softmax_scale must be > 0");
-  if ((reinterpret_cast<uintptr_t>(k) & 15) || ((k_sb | k_ss | k_sh) & 7) ||
-      (reinterpret_cast<uintptr_t>(v) & 7) || ((v_sb | v_ss | v_sh) & 3))
-    return fail(TG_ERR_ALIGNMENT, "decode_attn: k 16-byte aligned with strides multiples of 8 elements, "
-                                  "v 8-byte aligned with strides multiples of 4");
+  if (((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) ||
+      ((k_sb | k_ss | k_sh | v_sb | v_ss | v_sh) & 7))
+    return fail(TG_ERR_ALIGNMENT, "decode_attn: k and v 16-byte aligned with strides multiples of 8 elements");
   const int nc = decode_chunks(n_keys);
   if (nc > 1) {
     const size_t need = (size_t)B * Hq * nc * tg::kDecPart * sizeof(float);
@@ -783,17 +783,38 @@ int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh, const float* q_
   p.n_chunks = nc;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev;
+  int st = current_device(&dev);
+  if (st) return st;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_dec_attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(tg::decode_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           tg::dec_smem_bytes<1>());
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tg::decode_attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 tg::dec_smem_bytes<2>());
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tg::decode_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 tg::dec_smem_bytes<4>());
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tg::decode_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 tg::dec_smem_bytes<8>());
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode attention smem)");
+      g_dec_attr_set[dev] = true;
+    }
+  }
   dim3 grid((unsigned)nc, (unsigned)Hkv, (unsigned)B);
   switch (G) {
-    case 1: tg::decode_attn_kernel<1><<<grid, tg::kDecThreads, 0, s>>>(p); break;
-    case 2: tg::decode_attn_kernel<2><<<grid, tg::kDecThreads, 0, s>>>(p); break;
-    case 4: tg::decode_attn_kernel<4><<<grid, tg::kDecThreads, 0, s>>>(p); break;
-    default: tg::decode_attn_kernel<8><<<grid, tg::kDecThreads, 0, s>>>(p); break;
+    case 1: tg::decode_attn_kernel<1><<<grid, tg::kDecThreads, tg::dec_smem_bytes<1>(), s>>>(p); break;
+    case 2: tg::decode_attn_kernel<2><<<grid, tg::kDecThreads, tg::dec_smem_bytes<2>(), s>>>(p); break;
+    case 4: tg::decode_attn_kernel<4><<<grid, tg::kDecThreads, tg::dec_smem_bytes<4>(), s>>>(p); break;
+    default: tg::decode_attn_kernel<8><<<grid, tg::kDecThreads, tg::dec_smem_bytes<8>(), s>>>(p); break;
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode_attn launch");
   if (nc > 1) {
-    tg::decode_combine_kernel<<<dim3((unsigned)Hq, (unsigned)B), tg::kDecD, 0, s>>>(p);
+    tg::decode_combine_kernel<<<dim3((unsigned)Hq, (unsigned)B), tg::kCombThreads, 0, s>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn combine launch");
   }
