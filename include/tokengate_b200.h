@@ -321,6 +321,18 @@ int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh,
                       void* workspace, size_t workspace_bytes,
                       int B, int Hq, int Hkv, int D, float softmax_scale, void* stream);
 
+/* f4 — decode projections: y[b, :] = x[b, :] W^T for B <= 8 rows (the
+ * decode step's tokens), x (B, K) bf16 row stride ld_x, W (N, K) bf16
+ * row-major row stride ld_w, y (B, N) bf16 row stride ld_y; K a multiple of
+ * 256; x and W 16-byte aligned with row strides multiples of 8. With swiglu
+ * != 0, W is the fused [gate; up] weight of 2N rows and
+ * y[b, j] = bf16(bf16(silu(bf16(g))) * bf16(u)) with g, u rows j and N + j —
+ * the decode layer's gate/up projection and SwiGLU in one pass.
+ * Replaces the decode step's projections (nn.Linear under the layers of
+ * tokengate/e2e_gate/decode/gate_decode.py:199-219) for small batches. */
+int tg_gemv(const void* x, int64_t ld_x, const void* w, int64_t ld_w, void* y, int64_t ld_y,
+            int B, int N, int K, int swiglu, void* stream);
+
 /* Scratch bytes tg_decode_attn needs (0: one key chunk, none). */
 int tg_decode_attn_workspace(int B, int Hq, int n_keys, size_t* bytes);
 

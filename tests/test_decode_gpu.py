@@ -203,3 +203,23 @@ def test_decode_graph_equals_eager(tiny, cuda):
     torch.cuda.synchronize()
     assert ops.device_error() == 0
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("B,N,K", [(1, 4096, 2048), (3, 2048, 6144), (8, 1000, 512), (5, 151936, 2048)])
+def test_gemv_vs_cublas(cuda, B, N, K):
+    """tg_gemv against torch's bf16 GEMM (cuBLAS): both accumulate in fp32 and
+    round once to bf16, in different orders, so outputs agree to one bf16
+    ulp (relative 2^-7 here, with an absolute floor for cancellations) and
+    nearly all bit for bit."""
+    g = torch.Generator(device=cuda).manual_seed(B * 7 + K)
+    x = torch.randn(B, K, device=cuda, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda, generator=g) / K ** 0.5).to(torch.bfloat16)
+    got = ops.gemv(x, w).float()
+    ref = torch.nn.functional.linear(x, w).float()
+    assert ((got - ref).abs() <= 2 ** -7 * ref.abs() + 2e-3).all()
+    assert (got == ref).float().mean().item() >= 0.95
+    if N % 16 == 0:   # the silu_mul reference takes an intermediate size that is a multiple of 8
+        act = ops.gemv(x, w, swiglu=True).float()
+        ref_act = ops.silu_mul(torch.nn.functional.linear(x, w)).float()
+        assert ((act - ref_act).abs() <= 2 ** -6 * ref_act.abs() + 2e-3).all()
+        assert (act == ref_act).float().mean().item() >= 0.9

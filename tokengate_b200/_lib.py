@@ -93,6 +93,7 @@ _SIGNATURES = {
     "tg_decode_attn_ex": [_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64,
                           _P, _I32, _I32, _P, _P, _I64, _I64, _P, ctypes.c_size_t, _I32, _I32, _I32, _I32, _F,
                           _P],
+    "tg_gemv": [_P, _I64, _P, _I64, _P, _I64, _I32, _I32, _I32, _I32, _P],
     "tg_decode_attn_workspace": [_I32, _I32, _I32, ctypes.POINTER(ctypes.c_size_t)],
     "tg_decode_attn_noalloc": [_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64,
                                _I64, _P, _I32, _I32, _P, _I64, _I64, _I32, _I32, _I32, _I32, _F, _P],

@@ -19,6 +19,7 @@
 #include "layer_glue.cuh"
 #include "e2e_gate.cuh"
 #include "decode_attn.cuh"
+#include "gemv.cuh"
 
 // Bit flags set by kernels whose bounded waits gave up (see ptx.cuh).
 __device__ unsigned int g_tg_device_error = 0;
@@ -129,6 +130,22 @@ int encode_bshd(CUtensorMap* map, const void* base, int B, int S, int H, int64_t
   return TG_OK;
 }
 
+}  // namespace
+
+namespace {
+template <int BT, bool SW>
+cudaError_t launch_gemv(const tg::GemvParams& p, cudaStream_t s) {
+  const int smem = BT * p.K * 2;
+  cudaError_t e = cudaFuncSetAttribute(tg::gemv_kernel<BT, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tg::gemv_kernel<BT, SW>, tg::kGemvThreads, smem);
+  if (e != cudaSuccess) return e;
+  const int64_t groups = (p.N + tg::kGemvWarps - 1) / tg::kGemvWarps;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(groups, (int64_t)sm_count() * std::max(per_sm, 1)));
+  tg::gemv_kernel<BT, SW><<<(unsigned)blocks, tg::kGemvThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
 }  // namespace
 
 extern "C" {
@@ -818,6 +835,41 @@ int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh, const float* q_
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn combine launch");
   }
+  return TG_OK;
+}
+
+
+int tg_gemv(const void* x, int64_t ld_x, const void* w, int64_t ld_w, void* y, int64_t ld_y, int B, int N, int K,
+            int swiglu, void* stream) {
+  if (x == nullptr || w == nullptr || y == nullptr) return fail(TG_ERR_INVALID_ARGUMENT, "gemv: NULL argument");
+  if (B < 1 || B > 8 || N < 1 || K < 256 || (K % 256) != 0)
+    return fail(TG_ERR_UNSUPPORTED, "gemv: B=%d (1..8 served), N=%d, K=%d (a multiple of 256 served)", B, N, K);
+  if (ld_x < K || ld_w < K || ld_y < N)
+    return fail(TG_ERR_INVALID_ARGUMENT, "gemv: row strides shorter than the rows");
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) || ((ld_x | ld_w) & 7))
+    return fail(TG_ERR_ALIGNMENT, "gemv: x and w 16-byte aligned with row strides multiples of 8");
+  if ((size_t)((B <= 1) ? 1 : (B <= 2) ? 2 : (B <= 4) ? 4 : 8) * K * 2 > 200 * 1024)
+    return fail(TG_ERR_UNSUPPORTED, "gemv: %d rows of K=%d do not fit shared memory", B, K);
+  tg::GemvParams p;
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ld_x = ld_x;
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.ld_w = ld_w;
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ld_y = ld_y;
+  p.B = B;
+  p.N = N;
+  p.K = K;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (swiglu) {
+    e = B <= 1 ? launch_gemv<1, true>(p, s) : B <= 2 ? launch_gemv<2, true>(p, s)
+        : B <= 4 ? launch_gemv<4, true>(p, s) : launch_gemv<8, true>(p, s);
+  } else {
+    e = B <= 1 ? launch_gemv<1, false>(p, s) : B <= 2 ? launch_gemv<2, false>(p, s)
+        : B <= 4 ? launch_gemv<4, false>(p, s) : launch_gemv<8, false>(p, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
   return TG_OK;
 }
 

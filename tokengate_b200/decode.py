@@ -35,7 +35,7 @@ import torch
 import torch.nn.functional as F
 
 from . import ops
-from .layers import fused_weights, layer_mlp
+from .layers import fused_weights
 from .prefill import prefill_batch_for_decode
 
 
@@ -54,6 +54,17 @@ class GateGenerateResult:
 def _sync(device) -> None:
     if device.type == "cuda":
         torch.cuda.synchronize(device)
+
+
+def _proj(x: torch.Tensor, w: torch.Tensor, swiglu: bool = False, gemv: bool = True) -> torch.Tensor:
+    """A decode-step projection of the (B, 1, K) rows: the tg_gemv kernel for
+    the few rows of a decode step (B <= 8, K a multiple of 256), cuBLAS above
+    or when gemv is False."""
+    B, _, Kd = x.shape
+    if gemv and B <= 8 and Kd % 256 == 0:
+        return ops.gemv(x.view(B, Kd), w, swiglu=swiglu).view(B, 1, -1)
+    y = F.linear(x, w)
+    return ops.silu_mul(y) if swiglu else y
 
 
 class _DecodeCache:
@@ -80,7 +91,8 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
                    max_new_tokens: int, *, eos_token_id: Optional[int] = None,
                    phase2_form: bool = True, prune_below_gate: bool = False,
                    streamer=None, forced_tokens: Optional[torch.Tensor] = None,
-                   logits_out: Optional[list] = None, use_graph: bool = True) -> GateGenerateResult:
+                   logits_out: Optional[list] = None, use_graph: bool = True,
+                   use_gemv: bool = True) -> GateGenerateResult:
     """Gated prefill + greedy decode of up to max_new_tokens tokens per row.
 
     forced_tokens: (B, max_new_tokens - 1) ids fed to the decode steps in
@@ -89,7 +101,8 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
     logits_out: a list that receives each decode step's (B, vocab) fp32 logits;
     use_graph: replay the decode step as one CUDA graph after the first
     (eager) step — the state a step reads (token, position, append slot, key
-    count) lives in device buffers the step itself advances."""
+    count) lives in device buffers the step itself advances; use_gemv: the
+    decode projections on the tg_gemv kernel (False: cuBLAS)."""
     if max_new_tokens < 1:
         raise ValueError("max_new_tokens must be positive")
     device = next(model.parameters()).device
@@ -153,7 +166,7 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
                 lw = fw[i]
                 below = i <= gate_layer
                 h, x = ops.add_rmsnorm(h, delta, lw.in_w, lw.eps, h_out=h if delta is not None else None)
-                qkv = F.linear(x, lw.wqkv).view(B, 1, nq + 2 * nkv, D)
+                qkv = _proj(x, lw.wqkv, gemv=use_gemv).view(B, 1, nq + 2 * nkv, D)
                 q = qkv[:, :, :nq]
                 k = qkv[:, :, nq:nq + nkv]
                 v = qkv[:, :, nq + nkv:]
@@ -168,11 +181,11 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
                     a = ops.decode_attention(q[:, 0], dc.k[i], dc.v[i], n_kept_dev, W, W + extra,
                                              bias=bias[li], q_scale=qs_cur[li] if qs_cur is not None else None,
                                              n_keys_dev=nk_2)
-                o = F.linear(a.view(B, 1, nq * D), lw.wo)
+                o = _proj(a.view(B, 1, nq * D), lw.wo, gemv=use_gemv)
                 h, x2 = ops.add_rmsnorm(h, o, lw.post_w, lw.eps, h_out=h)
-                delta = layer_mlp(lw, x2)
+                delta = _proj(_proj(x2, lw.wgu, swiglu=True, gemv=use_gemv), lw.wdown, gemv=use_gemv)
             _, hn = ops.add_rmsnorm(h, delta, inner.norm.weight, float(inner.norm.variance_epsilon))
-            lg = model.lm_head(hn)[:, -1]
+            lg = _proj(hn, model.lm_head.weight, gemv=use_gemv)[:, -1]
             lg_buf.copy_(lg)
             cur.copy_(lg.argmax(-1, keepdim=True))
             pos.add_(1)

@@ -7,7 +7,7 @@
     python -m tokengate_b200.microbench branch [--seq 32768] [--inter 6144] [--batch 1]
     python -m tokengate_b200.microbench tables [--k 2000] [--layers 26] [--hq 16] [--batch 1]
     python -m tokengate_b200.microbench decode [--seq 2768] [--batch 1] [--hq 16] [--hkv 8] [--no-bias]
-    python -m tokengate_b200.microbench generate [--seq 32768] [--k 2000] [--batch 1] [--new 64] [--gate linear|e2e]
+    python -m tokengate_b200.microbench generate [--seq 32768] [--k 2000] [--batch 1] [--new 64] [--gate linear|e2e] [--proj gemv|cublas]
 
 Prints one JSON line per run with the CUDA-event time per launch and the
 algorithmic FLOPs or bytes of one launch (attention: 4*B*Hq*D*S(S+1)/2;
@@ -71,6 +71,7 @@ def main(argv=None):
                                        "generate"))
     ap.add_argument("--new", type=int, default=64)
     ap.add_argument("--gate", default="linear", choices=("linear", "e2e"))
+    ap.add_argument("--proj", default="gemv", choices=("gemv", "cublas"))
     ap.add_argument("--inter", type=int, default=6144)
     ap.add_argument("--layers", type=int, default=26)
     ap.add_argument("--seq", type=int, default=32768)
@@ -109,11 +110,12 @@ def main(argv=None):
         gh = torch.Generator().manual_seed(1000)
         prompts = [torch.randint(0, vocab, (S,), generator=gh) for _ in range(B)]
         st0, st1 = 512, S - 256
-        run = lambda n: generate_batch(tm.model, tm.gate, prompts, [st0] * B, [st1] * B, 1, a.k, n)
+        run = lambda n: generate_batch(tm.model, tm.gate, prompts, [st0] * B, [st1] * B, 1, a.k, n,
+                                       use_gemv=a.proj == "gemv")
         run(4)
         run(a.new)
         r = run(a.new)
-        res.update(seq=S, k=a.k, gate=a.gate, new=a.new, prefill_ms=r.prefill_s * 1e3,
+        res.update(seq=S, k=a.k, gate=a.gate, proj=a.proj, new=a.new, prefill_ms=r.prefill_s * 1e3,
                    decode_ms_per_token=r.decode_s * 1e3 / max(r.steps, 1),
                    decode_tokens_per_s=B * r.steps / r.decode_s if r.steps else None)
     elif a.kernel == "attn":

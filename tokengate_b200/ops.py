@@ -582,3 +582,26 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_valid:
             ws.data_ptr() if ws is not None else None, nbytes.value,
             B, Hq, Hkv, D, float(softmax_scale), _stream(q)))
     return out
+
+
+# ----------------------------------------------------------------- decode projections
+def gemv(x: torch.Tensor, w: torch.Tensor, swiglu: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ w.T for the decode step's few rows (tg_gemv): x (B, K) bf16 with
+    B <= 8 and K a multiple of 256, w (N, K) bf16 (row-major, contiguous
+    rows). swiglu: w is the fused [gate; up] weight (2I, K) and the result is
+    bf16(bf16(silu(gate)) * up), (B, I)."""
+    _require_cuda("x", x, torch.bfloat16)
+    _require_cuda("w", w, torch.bfloat16)
+    if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1] or x.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError(f"x {tuple(x.shape)} (B, K) and w {tuple(w.shape)} (N, K) with contiguous rows")
+    B, K = x.shape
+    N = w.shape[0] // 2 if swiglu else w.shape[0]
+    if swiglu and w.shape[0] % 2:
+        raise ValueError("the fused [gate; up] weight has an even number of rows")
+    if out is None:
+        out = torch.empty((B, N), dtype=torch.bfloat16, device=x.device)
+    L = _lib.lib()
+    with _device_ctx(x):
+        _lib.check(L.tg_gemv(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
+                             B, N, K, int(bool(swiglu)), _stream(x)))
+    return out
