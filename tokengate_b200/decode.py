@@ -57,11 +57,13 @@ def _sync(device) -> None:
 
 
 def _proj(x: torch.Tensor, w: torch.Tensor, swiglu: bool = False, gemv: bool = True) -> torch.Tensor:
-    """A decode-step projection of the (B, 1, K) rows: the tg_gemv kernel for
-    the few rows of a decode step (B <= 8, K a multiple of 256), cuBLAS above
-    or when gemv is False."""
+    """A decode-step projection of the (B, 1, K) rows: the tg_gemv kernel
+    where it beats cuBLAS on B200 (measured: every projection at B <= 2, the
+    layer projections at B <= 4; its CUDA-core FMAs fall behind cuBLAS's
+    tensor cores beyond that, first on the 151936-row lm_head), cuBLAS
+    otherwise or when gemv is False."""
     B, _, Kd = x.shape
-    if gemv and B <= 8 and Kd % 256 == 0:
+    if gemv and Kd % 256 == 0 and (B <= 2 or (B <= 4 and w.shape[0] < 32768)):
         return ops.gemv(x.view(B, Kd), w, swiglu=swiglu).view(B, 1, -1)
     y = F.linear(x, w)
     return ops.silu_mul(y) if swiglu else y

@@ -7,6 +7,7 @@
     python -m tokengate_b200.microbench branch [--seq 32768] [--inter 6144] [--batch 1]
     python -m tokengate_b200.microbench tables [--k 2000] [--layers 26] [--hq 16] [--batch 1]
     python -m tokengate_b200.microbench decode [--seq 2768] [--batch 1] [--hq 16] [--hkv 8] [--no-bias]
+    python -m tokengate_b200.microbench gemv [--n 12288] [--hidden 2048] [--batch 1]
     python -m tokengate_b200.microbench generate [--seq 32768] [--k 2000] [--batch 1] [--new 64] [--gate linear|e2e] [--proj gemv|cublas]
 
 Prints one JSON line per run with the CUDA-event time per launch and the
@@ -68,7 +69,8 @@ def _graph_time(fn, n, reps, warmup=3):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=("attn", "score", "topk", "gather", "branch", "tables", "decode",
-                                       "generate"))
+                                       "generate", "gemv"))
+    ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--new", type=int, default=64)
     ap.add_argument("--gate", default="linear", choices=("linear", "e2e"))
     ap.add_argument("--proj", default="gemv", choices=("gemv", "cublas"))
@@ -101,6 +103,15 @@ def main(argv=None):
         byts = B * ((S + 1) * a.hkv * 128 * 2 * 2 + a.hq * 128 * 4 + (0 if a.no_bias else a.hq * S * 4))
         res.update(seq=S, hq=a.hq, hkv=a.hkv, bias=not a.no_bias, ms=ms, us=ms * 1e3, mbytes=byts / 1e6,
                    gbs=byts / ms / 1e6)
+    elif a.kernel == "gemv":
+        x = torch.randn(B, a.hidden, device=dev, dtype=torch.bfloat16, generator=g)
+        w = (torch.randn(a.n, a.hidden, device=dev, generator=g) / a.hidden ** 0.5).to(torch.bfloat16)
+        out = torch.empty(B, a.n, device=dev, dtype=torch.bfloat16)
+        ms = _graph_time(lambda: ops.gemv(x, w, out=out), 20, a.iters)
+        ms_ref = _graph_time(lambda: torch.nn.functional.linear(x, w), 20, a.iters)
+        byts = a.n * a.hidden * 2 + B * (a.hidden + a.n) * 2
+        res.update(n=a.n, k=a.hidden, ms=ms, us=ms * 1e3, mbytes=byts / 1e6, gbs=byts / ms / 1e6,
+                   cublas_us=ms_ref * 1e3, cublas_gbs=byts / ms_ref / 1e6)
     elif a.kernel == "generate":
         from .decode import generate_batch
         from .inference import load_model
