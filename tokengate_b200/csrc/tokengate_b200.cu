@@ -133,16 +133,26 @@ int encode_bshd(CUtensorMap* map, const void* base, int B, int S, int H, int64_t
 }  // namespace
 
 namespace {
+constexpr int kGemvMaxSmem = 200 * 1024;  // the rows of x in shared memory: BT * K * 2 bytes at most
+
+// One gemv launch: the kernel's shared-memory limit is raised once per device
+// (not per launch, so launches inside a stream capture issue no attribute
+// calls); two CTAs of 8 warps per SM, or fewer when there are fewer rows.
 template <int BT, bool SW>
-cudaError_t launch_gemv(const tg::GemvParams& p, cudaStream_t s) {
+cudaError_t launch_gemv(const tg::GemvParams& p, cudaStream_t s, int dev) {
+  static bool attr_set[kMaxDevices] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(tg::gemv_kernel<BT, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kGemvMaxSmem);
+      if (e != cudaSuccess) return e;
+      attr_set[dev] = true;
+    }
+  }
   const int smem = BT * p.K * 2;
-  cudaError_t e = cudaFuncSetAttribute(tg::gemv_kernel<BT, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tg::gemv_kernel<BT, SW>, tg::kGemvThreads, smem);
-  if (e != cudaSuccess) return e;
   const int64_t groups = (p.N + tg::kGemvWarps - 1) / tg::kGemvWarps;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(groups, (int64_t)sm_count() * std::max(per_sm, 1)));
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(groups, 2LL * sm_count()));
   tg::gemv_kernel<BT, SW><<<(unsigned)blocks, tg::kGemvThreads, smem, s>>>(p);
   return cudaGetLastError();
 }
@@ -848,7 +858,7 @@ int tg_gemv(const void* x, int64_t ld_x, const void* w, int64_t ld_w, void* y, i
     return fail(TG_ERR_INVALID_ARGUMENT, "gemv: row strides shorter than the rows");
   if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) || ((ld_x | ld_w) & 7))
     return fail(TG_ERR_ALIGNMENT, "gemv: x and w 16-byte aligned with row strides multiples of 8");
-  if ((size_t)((B <= 1) ? 1 : (B <= 2) ? 2 : (B <= 4) ? 4 : 8) * K * 2 > 200 * 1024)
+  if ((size_t)((B <= 1) ? 1 : (B <= 2) ? 2 : (B <= 4) ? 4 : 8) * K * 2 > (size_t)kGemvMaxSmem)
     return fail(TG_ERR_UNSUPPORTED, "gemv: %d rows of K=%d do not fit shared memory", B, K);
   tg::GemvParams p;
   p.x = static_cast<const __nv_bfloat16*>(x);
@@ -861,13 +871,16 @@ int tg_gemv(const void* x, int64_t ld_x, const void* w, int64_t ld_w, void* y, i
   p.N = N;
   p.K = K;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev;
+  int st = current_device(&dev);
+  if (st) return st;
   cudaError_t e;
   if (swiglu) {
-    e = B <= 1 ? launch_gemv<1, true>(p, s) : B <= 2 ? launch_gemv<2, true>(p, s)
-        : B <= 4 ? launch_gemv<4, true>(p, s) : launch_gemv<8, true>(p, s);
+    e = B <= 1 ? launch_gemv<1, true>(p, s, dev) : B <= 2 ? launch_gemv<2, true>(p, s, dev)
+        : B <= 4 ? launch_gemv<4, true>(p, s, dev) : launch_gemv<8, true>(p, s, dev);
   } else {
-    e = B <= 1 ? launch_gemv<1, false>(p, s) : B <= 2 ? launch_gemv<2, false>(p, s)
-        : B <= 4 ? launch_gemv<4, false>(p, s) : launch_gemv<8, false>(p, s);
+    e = B <= 1 ? launch_gemv<1, false>(p, s, dev) : B <= 2 ? launch_gemv<2, false>(p, s, dev)
+        : B <= 4 ? launch_gemv<4, false>(p, s, dev) : launch_gemv<8, false>(p, s, dev);
   }
   if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
   return TG_OK;
