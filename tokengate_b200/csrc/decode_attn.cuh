@@ -66,6 +66,11 @@ struct DecodeParams {
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// Launched with programmatic stream serialization: before the wait for the
+// kernel that appends this step's key, the chunk's prefix rows (those below
+// n_prefix, allocated in every caller's cache) are only prefetched into L2,
+// which cannot return stale data; q, the key count, every cache row, the
+// bias and the outputs are read or written after the wait.
 template <int G>
 __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(const DecodeParams p) {
   extern __shared__ __align__(16) uint8_t dsm[];
@@ -78,6 +83,13 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(const DecodePa
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int j0 = chunk * kDecKeys;
+  if (j0 + t < p.n_prefix) {
+    const int64_t j = j0 + t;
+    prefetch_l2_bulk(p.k + (int64_t)b * p.k_sb + j * p.k_ss + (int64_t)kvh * p.k_sh, 256u);
+    prefetch_l2_bulk(p.v + (int64_t)b * p.v_sb + j * p.v_ss + (int64_t)kvh * p.v_sh, 256u);
+  }
+  griddep_wait();
+  griddep_launch_dependents();
   const int n_keys = p.n_keys_dev != nullptr ? min(__ldg(p.n_keys_dev), p.n_keys) : p.n_keys;
   const int kend = min(kDecKeys, n_keys - j0);  // keys of this chunk (<= 0: none)
 
@@ -236,6 +248,8 @@ __global__ void __launch_bounds__(kCombThreads) decode_combine_kernel(const Deco
   __shared__ float red[kCombThreads / 32];
   __shared__ float part_o[kCombThreads / 32][kDecD];
   __shared__ float part_l[kCombThreads / 32];
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const float* rec = p.part + ((int64_t)b * p.Hq + h) * p.n_chunks * kDecPart;
   float m = -INFINITY;

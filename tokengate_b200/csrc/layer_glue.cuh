@@ -48,6 +48,8 @@ struct RmsParams {
 // one warp per row; NV 16-byte vectors (8 elements) per lane, hidden = 256 * NV
 template <int NV>
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const RmsParams p) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t warp_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -56,6 +58,15 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const RmsParams p) {
     const uint4* hin = reinterpret_cast<const uint4*>(p.h_in + row * p.ld_h_in);
 #pragma unroll
     for (int i = 0; i < NV; ++i) hv[i] = ld_nc_v4(hin + lane + 32 * i);
+    // up to hidden 2048 the gains are loaded with the row (one round trip
+    // less on the few-row decode path); wider rows load them after the sum
+    constexpr bool kEarlyW = NV <= 8;
+    const uint4* wv = reinterpret_cast<const uint4*>(p.w);
+    uint4 wgt[kEarlyW ? NV : 1];
+    if (kEarlyW && p.x_out != nullptr) {
+#pragma unroll
+      for (int i = 0; i < (kEarlyW ? NV : 1); ++i) wgt[i] = __ldg(wv + lane + 32 * i);
+    }
     if (p.delta != nullptr) {
       const uint4* din = reinterpret_cast<const uint4*>(p.delta + row * p.ld_delta);
 #pragma unroll
@@ -85,11 +96,10 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const RmsParams p) {
     }
     ss = warp_sum(ss);
     const float inv = rsqrtf(ss * p.inv_hidden + p.eps);
-    const uint4* wv = reinterpret_cast<const uint4*>(p.w);
     uint4* xo = reinterpret_cast<uint4*>(p.x_out + row * p.ld_x);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const uint4 ww = __ldg(wv + lane + 32 * i);
+      const uint4 ww = kEarlyW ? wgt[kEarlyW ? i : 0] : __ldg(wv + lane + 32 * i);
       const uint32_t* a = reinterpret_cast<const uint32_t*>(&hv[i]);
       const uint32_t* w = reinterpret_cast<const uint32_t*>(&ww);
       uint4 o;
@@ -125,10 +135,12 @@ struct QkRopeParams {
   __nv_bfloat16* v_cache;
   int64_t kc_sb, kc_ss;
   const int64_t* slot_dev;
+  int split;                   // warps per row: each takes every split-th group of 2 * kQkBatch heads
 };
 
-// One warp per row: the row's cos / sin and the two norm gains are loaded
-// once, then each half-warp takes every other head of the row, up to
+// One warp per row (with few rows, `split` warps per row, each taking every
+// split-th group of heads): the row's cos / sin and the two norm gains are
+// loaded once, then each half-warp takes every other head of the row, up to
 // kQkBatch heads per half with every load issued before any arithmetic. Lane
 // l of a half holds elements 4l..4l+3 of its head and their rotate-half
 // partners 64+4l..64+4l+3 (two 8-byte loads), so the rotation needs no
@@ -196,7 +208,11 @@ __device__ __forceinline__ float qk_sumsq(const uint2 xl, const uint2 xh) {
   return ss;
 }
 
+// Launched with programmatic stream serialization (the norm gains are read
+// after the wait too: a caller may have just written them).
 __global__ void __launch_bounds__(256, 3) qk_norm_rope_kernel(const QkRopeParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int hl = lane & 15;    // lane inside the half-warp
   const int half = lane >> 4;  // heads half, half + 2, half + 4, ...
@@ -207,7 +223,10 @@ __global__ void __launch_bounds__(256, 3) qk_norm_rope_kernel(const QkRopeParams
   const uint2* kwp = reinterpret_cast<const uint2*>(p.k_w);
   const uint2 qwl = __ldg(qwp + hl), qwh = __ldg(qwp + 16 + hl);
   const uint2 kwl = __ldg(kwp + hl), kwh = __ldg(kwp + 16 + hl);
-  for (int64_t row = warp_global; row < p.rows; row += n_warps) {
+  const int64_t n_items = p.rows * p.split;
+  for (int64_t item = warp_global; item < n_items; item += n_warps) {
+    const int64_t row = p.split == 1 ? item : item / p.split;
+    const int gsel = (int)(item - row * p.split);
     const int64_t b = row / p.seq, s = row - b * p.seq;
     QkRow cs;
     {
@@ -226,9 +245,9 @@ __global__ void __launch_bounds__(256, 3) qk_norm_rope_kernel(const QkRopeParams
       const int64_t slot = __ldg(p.slot_dev);
       kcrow = p.k_cache + row * p.kc_sb + slot * p.kc_ss;
       vcrow = p.v_cache + row * p.kc_sb + slot * p.kc_ss;
-      // v heads: straight copy into the cache
+      // v heads: straight copy into the cache (by the row's first warp)
       const uint2* vrow = reinterpret_cast<const uint2*>(p.v + row * p.ld_v);
-      for (int hd = half; hd < p.n_k; hd += 2) {
+      for (int hd = half; gsel == 0 && hd < p.n_k; hd += 2) {
         const uint2 a = vrow[hd * 32 + hl], c = vrow[hd * 32 + 16 + hl];
         uint2* dst = reinterpret_cast<uint2*>(vcrow + (int64_t)hd * 128);
         dst[hl] = a;
@@ -236,7 +255,7 @@ __global__ void __launch_bounds__(256, 3) qk_norm_rope_kernel(const QkRopeParams
       }
     }
     // the head loop is uniform across the warp (the shuffles need every lane)
-    for (int h0 = 0; h0 < heads; h0 += 2 * kQkBatch) {
+    for (int h0 = gsel * 2 * kQkBatch; h0 < heads; h0 += p.split * 2 * kQkBatch) {
       uint2 xl[kQkBatch], xh[kQkBatch];
       float ss[kQkBatch];
 #pragma unroll
@@ -288,6 +307,8 @@ struct SiluParams {
 };
 
 __global__ void __launch_bounds__(256) silu_mul_kernel(const SiluParams p) {
+  griddep_wait();  // launched with programmatic stream serialization
+  griddep_launch_dependents();
   const int64_t vec_per_row = p.inter >> 3;
   const int64_t total = p.rows * vec_per_row;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;

@@ -263,10 +263,31 @@ __device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may begin while the kernel before it in the stream is still
+// running. griddep_wait() blocks until that predecessor has completed and
+// its memory writes are visible (for an ordinary launch it returns at once);
+// a kernel so launched reads and writes nothing that another kernel writes
+// or reads before it. Its memory clobber orders plain loads and stores after
+// it; the library's inline-asm loads are volatile (as __ldg is), so they
+// stay after it too. griddep_launch_dependents() lets the next such kernel
+// start early; each kernel here calls it only after its own wait, so at most
+// two kernels of a chain overlap.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Bulk prefetch of [ptr, ptr + bytes) into L2 (16-byte aligned, bytes a
+// multiple of 16): for data no earlier kernel writes, issued before the wait.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* ptr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
+}
+
 // 16-byte read-only global load that does not allocate in L1 (streamed data).
+// Volatile, like __ldg: never scheduled ahead of an earlier griddep_wait().
 __device__ __forceinline__ uint4 ld_nc_v4(const uint4* ptr) {
   uint4 v;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
       : "l"(ptr));
   return v;

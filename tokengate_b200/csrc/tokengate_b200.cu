@@ -133,6 +133,27 @@ int encode_bshd(CUtensorMap* map, const void* base, int B, int S, int H, int64_t
 }  // namespace
 
 namespace {
+// Launch with programmatic stream serialization, for the kernels of the
+// layer chains (layer glue, decode attention, gemv): the kernel may start
+// while the previous kernel on the stream drains, and waits on the device
+// (griddep_wait) before it touches anything that kernel writes. Under a
+// stream capture this becomes a programmatic edge of the graph.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 constexpr int kGemvMaxSmem = 200 * 1024;  // the rows of x in shared memory: BT * K * 2 bytes at most
 
 // One gemv launch: the kernel's shared-memory limit is raised once per device
@@ -153,8 +174,7 @@ cudaError_t launch_gemv(const tg::GemvParams& p, cudaStream_t s, int dev) {
   const int smem = BT * p.K * 2;
   const int64_t groups = (p.N + tg::kGemvWarps - 1) / tg::kGemvWarps;
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(groups, 2LL * sm_count()));
-  tg::gemv_kernel<BT, SW><<<(unsigned)blocks, tg::kGemvThreads, smem, s>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(tg::gemv_kernel<BT, SW>, dim3((unsigned)blocks), dim3(tg::kGemvThreads), (size_t)smem, s, p);
 }
 }  // namespace
 
@@ -481,16 +501,17 @@ int tg_add_rmsnorm(const void* h_in, int64_t ld_h_in, const void* delta, int64_t
   p.inv_hidden = 1.f / (float)hidden;
   const int64_t blocks = resident_blocks((rows + 7) / 8, 8);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)blocks), block(256);
+  cudaError_t e;
   switch (nv) {
-    case 1: tg::add_rmsnorm_kernel<1><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-    case 2: tg::add_rmsnorm_kernel<2><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-    case 4: tg::add_rmsnorm_kernel<4><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-    case 8: tg::add_rmsnorm_kernel<8><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-    case 10: tg::add_rmsnorm_kernel<10><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-    case 16: tg::add_rmsnorm_kernel<16><<<(unsigned)blocks, 256, 0, s>>>(p); break;
-    default: tg::add_rmsnorm_kernel<20><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+    case 1: e = launch_pdl(tg::add_rmsnorm_kernel<1>, grid, block, 0, s, p); break;
+    case 2: e = launch_pdl(tg::add_rmsnorm_kernel<2>, grid, block, 0, s, p); break;
+    case 4: e = launch_pdl(tg::add_rmsnorm_kernel<4>, grid, block, 0, s, p); break;
+    case 8: e = launch_pdl(tg::add_rmsnorm_kernel<8>, grid, block, 0, s, p); break;
+    case 10: e = launch_pdl(tg::add_rmsnorm_kernel<10>, grid, block, 0, s, p); break;
+    case 16: e = launch_pdl(tg::add_rmsnorm_kernel<16>, grid, block, 0, s, p); break;
+    default: e = launch_pdl(tg::add_rmsnorm_kernel<20>, grid, block, 0, s, p); break;
   }
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "add_rmsnorm launch");
   return TG_OK;
 }
@@ -555,9 +576,13 @@ static int qk_norm_rope_impl(void* q, int64_t ld_q, int n_q_heads, void* k, int6
     p.kc_ss = append->kc_ss;
     p.slot_dev = append->slot_dev;
   }
-  const int64_t blocks = resident_blocks((rows + 7) / 8, 8);  // one warp per row
-  tg::qk_norm_rope_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  cudaError_t e = cudaGetLastError();
+  // one warp per row; with few rows (decode) one warp per group of
+  // 2 * kQkBatch heads of a row, so the heads are not done one group after another
+  const int groups = (n_q_heads + n_k_heads + 2 * tg::kQkBatch - 1) / (2 * tg::kQkBatch);
+  p.split = rows <= 64 ? groups : 1;
+  const int64_t blocks = resident_blocks((rows * p.split + 7) / 8, 8);
+  cudaError_t e = launch_pdl(tg::qk_norm_rope_kernel, dim3((unsigned)blocks), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), p);
   if (e != cudaSuccess) return cuda_fail(e, "qk_norm_rope launch");
   return TG_OK;
 }
@@ -603,8 +628,8 @@ int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_
   p.ld_gu = ld_gu;
   p.ld_out = ld_out;
   const int64_t blocks = resident_blocks((rows * (inter / 8) + 255) / 256, 8);
-  tg::silu_mul_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(tg::silu_mul_kernel, dim3((unsigned)blocks), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), p);
   if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
   return TG_OK;
 }
@@ -832,17 +857,17 @@ int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh, const float* q_
     }
   }
   dim3 grid((unsigned)nc, (unsigned)Hkv, (unsigned)B);
+  const dim3 block(tg::kDecThreads);
+  cudaError_t e;
   switch (G) {
-    case 1: tg::decode_attn_kernel<1><<<grid, tg::kDecThreads, tg::dec_smem_bytes<1>(), s>>>(p); break;
-    case 2: tg::decode_attn_kernel<2><<<grid, tg::kDecThreads, tg::dec_smem_bytes<2>(), s>>>(p); break;
-    case 4: tg::decode_attn_kernel<4><<<grid, tg::kDecThreads, tg::dec_smem_bytes<4>(), s>>>(p); break;
-    default: tg::decode_attn_kernel<8><<<grid, tg::kDecThreads, tg::dec_smem_bytes<8>(), s>>>(p); break;
+    case 1: e = launch_pdl(tg::decode_attn_kernel<1>, grid, block, tg::dec_smem_bytes<1>(), s, p); break;
+    case 2: e = launch_pdl(tg::decode_attn_kernel<2>, grid, block, tg::dec_smem_bytes<2>(), s, p); break;
+    case 4: e = launch_pdl(tg::decode_attn_kernel<4>, grid, block, tg::dec_smem_bytes<4>(), s, p); break;
+    default: e = launch_pdl(tg::decode_attn_kernel<8>, grid, block, tg::dec_smem_bytes<8>(), s, p); break;
   }
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode_attn launch");
   if (nc > 1) {
-    tg::decode_combine_kernel<<<dim3((unsigned)Hq, (unsigned)B), tg::kCombThreads, 0, s>>>(p);
-    e = cudaGetLastError();
+    e = launch_pdl(tg::decode_combine_kernel, dim3((unsigned)Hq, (unsigned)B), dim3(tg::kCombThreads), 0, s, p);
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn combine launch");
   }
   return TG_OK;
