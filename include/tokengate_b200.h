@@ -333,25 +333,6 @@ int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh,
 int tg_gemv(const void* x, int64_t ld_x, const void* w, int64_t ld_w, void* y, int64_t ld_y,
             int B, int N, int K, int swiglu, void* stream);
 
-/*
- * tg_add_rmsnorm followed by tg_gemv on its x, in one launch: the residual
- * add before a decode layer's attention (or MLP, or the final norm) and the
- * projection after it (q/k/v, gate/up, lm_head). h_out = bf16(h_in + delta)
- * when delta is non-NULL (h_in is left as it is); x = the RMSNorm of that
- * row with gain norm_w and eps, bit-identical to tg_add_rmsnorm's x_out and
- * never written to memory; y = x W^T as in tg_gemv (swiglu likewise). h_in,
- * delta, h_out: (B, K) bf16 rows, 16-byte aligned, strides multiples of 8;
- * h_out must be a buffer other than h_in and delta (every CTA reads them
- * while the first CTA writes h_out). The other arguments and limits are
- * tg_gemv's. Replaces the RMSNorm + projection pairs of the decode layers
- * (transformers Qwen3DecoderLayer input/post-attention norms and the final
- * norm before lm_head, under tokengate/e2e_gate/decode/gate_decode.py:199-219).
- */
-int tg_gemv_rmsnorm(const void* h_in, int64_t ld_h_in, const void* delta, int64_t ld_delta,
-                    void* h_out, int64_t ld_h_out, const void* norm_w, float eps, const void* w,
-                    int64_t ld_w, void* y, int64_t ld_y, int B, int N, int K, int swiglu,
-                    void* stream);
-
 /* Scratch bytes tg_decode_attn needs (0: one key chunk, none). */
 int tg_decode_attn_workspace(int B, int Hq, int n_keys, size_t* bytes);
 

@@ -19,7 +19,6 @@ import torch
 import oracle.decode as odec
 import oracle.prefill as opre
 from tokengate_b200 import ops
-from tokengate_b200._lib import TokenGateArgumentError
 from tokengate_b200.decode import generate_batch
 from tokengate_b200.gate import LinLogSigGate, synthetic_e2e_gate
 from tokengate_b200.inference import TokenGateModel, with_state_span
@@ -224,54 +223,3 @@ def test_gemv_vs_cublas(cuda, B, N, K):
         ref_act = ops.silu_mul(torch.nn.functional.linear(x, w)).float()
         assert ((act - ref_act).abs() <= 2 ** -6 * ref_act.abs() + 2e-3).all()
         assert (act == ref_act).float().mean().item() >= 0.9
-
-
-@pytest.mark.parametrize("B,N,K,with_delta,swiglu", [(1, 4096, 2048, True, False), (1, 3000, 2048, False, False),
-                                                     (2, 12288, 2048, True, True), (3, 2048, 4096, True, False),
-                                                     (8, 640, 1024, True, True)])
-def test_gemv_rmsnorm_matches_add_rmsnorm_then_gemv(cuda, B, N, K, with_delta, swiglu):
-    """tg_gemv_rmsnorm makes x in shared memory with tg_add_rmsnorm's
-    arithmetic and order, so h_out and y are bit-identical to add_rmsnorm
-    followed by gemv; h_in is left unchanged."""
-    g = torch.Generator(device=cuda).manual_seed(B * 13 + N)
-    h = torch.randn(B, K, device=cuda, generator=g).to(torch.bfloat16)
-    d = torch.randn(B, K, device=cuda, generator=g).to(torch.bfloat16) if with_delta else None
-    nw = (1 + 0.1 * torch.randn(K, device=cuda, generator=g)).to(torch.bfloat16)
-    w = (torch.randn(N, K, device=cuda, generator=g) / K ** 0.5).to(torch.bfloat16)
-    h0 = h.clone()
-    ho, y = ops.gemv_rmsnorm(h, d, nw, 1e-6, w, swiglu=swiglu)
-    ref_h, x = ops.add_rmsnorm(h0, d, nw, 1e-6)
-    ref_y = ops.gemv(x, w, swiglu=swiglu)
-    torch.cuda.synchronize()
-    assert torch.equal(h, h0)
-    assert torch.equal(ho, ref_h)
-    assert torch.equal(y, ref_y)
-
-
-def test_gemv_rmsnorm_rejects_in_place_residual(cuda):
-    h = torch.zeros(1, 2048, dtype=torch.bfloat16, device=cuda)
-    w = torch.zeros(64, 2048, dtype=torch.bfloat16, device=cuda)
-    nw = torch.ones(2048, dtype=torch.bfloat16, device=cuda)
-    with pytest.raises(TokenGateArgumentError, match="other than h_in"):
-        ops.gemv_rmsnorm(h, h.clone(), nw, 1e-6, w, h_out=h)
-
-
-def test_decode_fused_norm_equals_separate(tiny, cuda, monkeypatch):
-    """The decode step with each residual add + RMSNorm fused into the
-    projection after it (tg_gemv_rmsnorm) gives the logits of the separate
-    add_rmsnorm + gemv launches bit for bit."""
-    import tokengate_b200.decode as dec
-    g = torch.Generator().manual_seed(29)
-    prompts = [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (260, 310)]
-    gate = LinLogSigGate(512).to(cuda)
-    forced = torch.randint(0, 1000, (2, 5), generator=g)
-    outs = []
-    for fuse in (False, True):
-        monkeypatch.setattr(dec, "_FUSE_NORM", fuse)
-        lg = []
-        generate_batch(tiny["model"], gate, prompts, [10, 20], [240, 290], 1, 40, 6, forced_tokens=forced,
-                       logits_out=lg)
-        outs.append(torch.stack(lg))
-    torch.cuda.synchronize()
-    assert ops.device_error() == 0
-    assert torch.equal(outs[0], outs[1])

@@ -94,7 +94,6 @@ _SIGNATURES = {
                           _P, _I32, _I32, _P, _P, _I64, _I64, _P, ctypes.c_size_t, _I32, _I32, _I32, _I32, _F,
                           _P],
     "tg_gemv": [_P, _I64, _P, _I64, _P, _I64, _I32, _I32, _I32, _I32, _P],
-    "tg_gemv_rmsnorm": [_P, _I64, _P, _I64, _P, _I64, _P, _F, _P, _I64, _P, _I64, _I32, _I32, _I32, _I32, _P],
     "tg_decode_attn_workspace": [_I32, _I32, _I32, ctypes.POINTER(ctypes.c_size_t)],
     "tg_decode_attn_noalloc": [_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64,
                                _I64, _P, _I32, _I32, _P, _I64, _I64, _I32, _I32, _I32, _I32, _F, _P],

@@ -16,7 +16,6 @@
 
 #include "ptx.cuh"
 #include "e2e_gate.cuh"  // bf16_round
-#include "layer_glue.cuh"  // bf16 packing helpers shared with add_rmsnorm_kernel
 
 namespace tg {
 
@@ -31,71 +30,7 @@ struct GemvParams {
   __nv_bfloat16* y;
   int64_t ld_y;
   int B, N, K;   // N: output columns (SwiGLU: the intermediate size I; W has 2I rows)
-  // Optional fused residual add + RMSNorm (norm_w non-null; x unused): the
-  // rows of x are made in shared memory exactly as add_rmsnorm_kernel makes
-  // them, a = bf16(h_in + delta) (a = h_in without delta) and
-  // x = bf16(norm_w * bf16(a * rsqrt(mean(a^2) + eps))); CTA 0 writes a to
-  // h_out (every CTA reads h_in and delta, so h_out is a third buffer).
-  const __nv_bfloat16* h_in;
-  int64_t ld_h_in;
-  const __nv_bfloat16* delta;
-  int64_t ld_delta;
-  __nv_bfloat16* h_out;
-  int64_t ld_h_out;
-  const __nv_bfloat16* norm_w;
-  float eps, inv_hidden;
 };
-
-// Row b of x into shared memory through the residual add + RMSNorm, by one
-// warp, with add_rmsnorm_kernel's lane mapping (lane l: 16-byte vectors
-// l, l + 32, ...) and its order of operations, so x is bit-identical to the
-// x_out that kernel writes.
-__device__ __forceinline__ void gemv_norm_row(const GemvParams& p, __nv_bfloat16* xs_row, int b, int lane) {
-  const int nvr = p.K / 256;
-  const uint4* hin = reinterpret_cast<const uint4*>(p.h_in + (int64_t)b * p.ld_h_in);
-  const uint4* din = p.delta != nullptr ? reinterpret_cast<const uint4*>(p.delta + (int64_t)b * p.ld_delta) : nullptr;
-  uint4* hout = (p.delta != nullptr && blockIdx.x == 0) ? reinterpret_cast<uint4*>(p.h_out + (int64_t)b * p.ld_h_out)
-                                                          : nullptr;
-  uint4* xr = reinterpret_cast<uint4*>(xs_row);
-  float ss = 0.f;
-  for (int i = 0; i < nvr; ++i) {
-    uint4 hv = ld_nc_v4(hin + lane + 32 * i);
-    if (din != nullptr) {
-      const uint4 dv = ld_nc_v4(din + lane + 32 * i);
-      uint32_t* a = reinterpret_cast<uint32_t*>(&hv);
-      const uint32_t* d = reinterpret_cast<const uint32_t*>(&dv);
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        a[e] = pack_bf16x2(bf16_lo(a[e]) + bf16_lo(d[e]), bf16_hi(a[e]) + bf16_hi(d[e]));
-      if (hout != nullptr) hout[lane + 32 * i] = hv;
-    }
-    const uint32_t* a = reinterpret_cast<const uint32_t*>(&hv);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float lo = bf16_lo(a[e]), hi = bf16_hi(a[e]);
-      ss = fmaf(lo, lo, ss);
-      ss = fmaf(hi, hi, ss);
-    }
-    xr[lane + 32 * i] = hv;
-  }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  const float inv = rsqrtf(ss * p.inv_hidden + p.eps);
-  const uint4* wv = reinterpret_cast<const uint4*>(p.norm_w);
-  for (int i = 0; i < nvr; ++i) {
-    const uint4 ww = __ldg(wv + lane + 32 * i);
-    const uint4 hv = xr[lane + 32 * i];
-    const uint32_t* a = reinterpret_cast<const uint32_t*>(&hv);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&ww);
-    uint4 o;
-    uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      ov[e] = pack_bf16x2(bf16_lo(w[e]) * round_bf16(bf16_lo(a[e]) * inv),
-                          bf16_hi(w[e]) * round_bf16(bf16_hi(a[e]) * inv));
-    xr[lane + 32 * i] = o;
-  }
-}
 
 __device__ __forceinline__ float gemv_silu(float g) {
   // the eager op: g / (1 + exp(-g)) in fp32, IEEE division
@@ -144,21 +79,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
   uint4 wv[R][kGemvBatch];
   if (warp_global < p.N) gemv_load_batch<R>(wv, w, p, warp_global, 0, n_slices, lane);
   // x rows into shared memory (rows past B are zero)
-  if (p.norm_w != nullptr) {
-    if (warp < BT) {
-      if (warp < p.B) {
-        gemv_norm_row(p, xs + (int64_t)warp * K, warp, lane);
-      } else {
-        for (int c = lane; c < K / 8; c += 32) reinterpret_cast<uint4*>(xs + (int64_t)warp * K)[c] = make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
-  } else {
-    for (int i = t; i < BT * (K / 8); i += kGemvThreads) {
-      const int b = i / (K / 8), c = i - b * (K / 8);
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (b < p.B) v = *reinterpret_cast<const uint4*>(x + (int64_t)b * p.ld_x + 8 * c);
-      reinterpret_cast<uint4*>(xs + (int64_t)b * K)[c] = v;
-    }
+  for (int i = t; i < BT * (K / 8); i += kGemvThreads) {
+    const int b = i / (K / 8), c = i - b * (K / 8);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (b < p.B) v = *reinterpret_cast<const uint4*>(x + (int64_t)b * p.ld_x + 8 * c);
+    reinterpret_cast<uint4*>(xs + (int64_t)b * K)[c] = v;
   }
   __syncthreads();
   griddep_launch_dependents();

@@ -176,41 +176,6 @@ cudaError_t launch_gemv(const tg::GemvParams& p, cudaStream_t s, int dev) {
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(groups, 2LL * sm_count()));
   return launch_pdl(tg::gemv_kernel<BT, SW>, dim3((unsigned)blocks), dim3(tg::kGemvThreads), (size_t)smem, s, p);
 }
-
-// The checks and launch shared by tg_gemv and tg_gemv_rmsnorm (p holds the
-// x source: x, or the fused residual add + RMSNorm inputs).
-int gemv_launch(tg::GemvParams& p, const void* w, int64_t ld_w, void* y, int64_t ld_y, int B, int N, int K,
-                int swiglu, void* stream) {
-  if (w == nullptr || y == nullptr) return fail(TG_ERR_INVALID_ARGUMENT, "gemv: NULL argument");
-  if (B < 1 || B > 8 || N < 1 || K < 256 || (K % 256) != 0)
-    return fail(TG_ERR_UNSUPPORTED, "gemv: B=%d (1..8 served), N=%d, K=%d (a multiple of 256 served)", B, N, K);
-  if (ld_w < K || ld_y < N) return fail(TG_ERR_INVALID_ARGUMENT, "gemv: row strides shorter than the rows");
-  if ((reinterpret_cast<uintptr_t>(w) & 15) || (ld_w & 7))
-    return fail(TG_ERR_ALIGNMENT, "gemv: x and w 16-byte aligned with row strides multiples of 8");
-  if ((size_t)((B <= 1) ? 1 : (B <= 2) ? 2 : (B <= 4) ? 4 : 8) * K * 2 > (size_t)kGemvMaxSmem)
-    return fail(TG_ERR_UNSUPPORTED, "gemv: %d rows of K=%d do not fit shared memory", B, K);
-  p.w = static_cast<const __nv_bfloat16*>(w);
-  p.ld_w = ld_w;
-  p.y = static_cast<__nv_bfloat16*>(y);
-  p.ld_y = ld_y;
-  p.B = B;
-  p.N = N;
-  p.K = K;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int dev;
-  int st = current_device(&dev);
-  if (st) return st;
-  cudaError_t e;
-  if (swiglu) {
-    e = B <= 1 ? launch_gemv<1, true>(p, s, dev) : B <= 2 ? launch_gemv<2, true>(p, s, dev)
-        : B <= 4 ? launch_gemv<4, true>(p, s, dev) : launch_gemv<8, true>(p, s, dev);
-  } else {
-    e = B <= 1 ? launch_gemv<1, false>(p, s, dev) : B <= 2 ? launch_gemv<2, false>(p, s, dev)
-        : B <= 4 ? launch_gemv<4, false>(p, s, dev) : launch_gemv<8, false>(p, s, dev);
-  }
-  if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
-  return TG_OK;
-}
 }  // namespace
 
 extern "C" {
@@ -911,41 +876,39 @@ int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh, const float* q_
 
 int tg_gemv(const void* x, int64_t ld_x, const void* w, int64_t ld_w, void* y, int64_t ld_y, int B, int N, int K,
             int swiglu, void* stream) {
-  if (x == nullptr) return fail(TG_ERR_INVALID_ARGUMENT, "gemv: NULL argument");
-  if (ld_x < K) return fail(TG_ERR_INVALID_ARGUMENT, "gemv: row strides shorter than the rows");
-  if ((reinterpret_cast<uintptr_t>(x) & 15) || (ld_x & 7))
+  if (x == nullptr || w == nullptr || y == nullptr) return fail(TG_ERR_INVALID_ARGUMENT, "gemv: NULL argument");
+  if (B < 1 || B > 8 || N < 1 || K < 256 || (K % 256) != 0)
+    return fail(TG_ERR_UNSUPPORTED, "gemv: B=%d (1..8 served), N=%d, K=%d (a multiple of 256 served)", B, N, K);
+  if (ld_x < K || ld_w < K || ld_y < N)
+    return fail(TG_ERR_INVALID_ARGUMENT, "gemv: row strides shorter than the rows");
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) || ((ld_x | ld_w) & 7))
     return fail(TG_ERR_ALIGNMENT, "gemv: x and w 16-byte aligned with row strides multiples of 8");
-  tg::GemvParams p = {};
+  if ((size_t)((B <= 1) ? 1 : (B <= 2) ? 2 : (B <= 4) ? 4 : 8) * K * 2 > (size_t)kGemvMaxSmem)
+    return fail(TG_ERR_UNSUPPORTED, "gemv: %d rows of K=%d do not fit shared memory", B, K);
+  tg::GemvParams p;
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.ld_x = ld_x;
-  return gemv_launch(p, w, ld_w, y, ld_y, B, N, K, swiglu, stream);
-}
-
-int tg_gemv_rmsnorm(const void* h_in, int64_t ld_h_in, const void* delta, int64_t ld_delta, void* h_out,
-                    int64_t ld_h_out, const void* norm_w, float eps, const void* w, int64_t ld_w, void* y,
-                    int64_t ld_y, int B, int N, int K, int swiglu, void* stream) {
-  if (h_in == nullptr || norm_w == nullptr || (delta != nullptr && h_out == nullptr))
-    return fail(TG_ERR_INVALID_ARGUMENT, "gemv_rmsnorm: NULL argument");
-  if (delta != nullptr && (h_out == h_in || h_out == delta))
-    return fail(TG_ERR_INVALID_ARGUMENT, "gemv_rmsnorm: h_out must be a buffer other than h_in and delta "
-                                         "(every CTA reads them while the first writes h_out)");
-  if (ld_h_in < K || (delta != nullptr && (ld_delta < K || ld_h_out < K)))
-    return fail(TG_ERR_INVALID_ARGUMENT, "gemv_rmsnorm: row strides shorter than the rows");
-  const uintptr_t m = reinterpret_cast<uintptr_t>(h_in) | reinterpret_cast<uintptr_t>(delta) |
-                      reinterpret_cast<uintptr_t>(h_out) | reinterpret_cast<uintptr_t>(norm_w);
-  if ((m & 15) || ((ld_h_in | (delta != nullptr ? (ld_delta | ld_h_out) : 0)) & 7))
-    return fail(TG_ERR_ALIGNMENT, "gemv_rmsnorm: pointers 16-byte aligned, strides multiples of 8 needed");
-  tg::GemvParams p = {};
-  p.h_in = static_cast<const __nv_bfloat16*>(h_in);
-  p.ld_h_in = ld_h_in;
-  p.delta = static_cast<const __nv_bfloat16*>(delta);
-  p.ld_delta = ld_delta;
-  p.h_out = static_cast<__nv_bfloat16*>(h_out);
-  p.ld_h_out = ld_h_out;
-  p.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
-  p.eps = eps;
-  p.inv_hidden = 1.f / (float)K;
-  return gemv_launch(p, w, ld_w, y, ld_y, B, N, K, swiglu, stream);
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.ld_w = ld_w;
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ld_y = ld_y;
+  p.B = B;
+  p.N = N;
+  p.K = K;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev;
+  int st = current_device(&dev);
+  if (st) return st;
+  cudaError_t e;
+  if (swiglu) {
+    e = B <= 1 ? launch_gemv<1, true>(p, s, dev) : B <= 2 ? launch_gemv<2, true>(p, s, dev)
+        : B <= 4 ? launch_gemv<4, true>(p, s, dev) : launch_gemv<8, true>(p, s, dev);
+  } else {
+    e = B <= 1 ? launch_gemv<1, false>(p, s, dev) : B <= 2 ? launch_gemv<2, false>(p, s, dev)
+        : B <= 4 ? launch_gemv<4, false>(p, s, dev) : launch_gemv<8, false>(p, s, dev);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+  return TG_OK;
 }
 
 int tg_decode_attn_noalloc(const void* q, int64_t q_sb, int64_t q_sh, const float* q_scale, int64_t qs_sb,

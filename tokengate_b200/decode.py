@@ -63,34 +63,10 @@ def _proj(x: torch.Tensor, w: torch.Tensor, swiglu: bool = False, gemv: bool = T
     tensor cores beyond that, first on the 151936-row lm_head), cuBLAS
     otherwise or when gemv is False."""
     B, _, Kd = x.shape
-    if _gemv_serves(B, Kd, w.shape[0], gemv):
+    if gemv and Kd % 256 == 0 and (B <= 2 or (B <= 4 and w.shape[0] < 32768)):
         return ops.gemv(x.view(B, Kd), w, swiglu=swiglu).view(B, 1, -1)
     y = F.linear(x, w)
     return ops.silu_mul(y) if swiglu else y
-
-
-def _gemv_serves(B: int, K: int, N: int, gemv: bool) -> bool:
-    return gemv and K % 256 == 0 and (B <= 2 or (B <= 4 and N < 32768))
-
-
-# the residual add + RMSNorm fused into the projection that follows it
-# (tg_gemv_rmsnorm) wherever the GEMV serves that projection
-_FUSE_NORM = True
-
-
-def _norm_proj(h: torch.Tensor, delta: Optional[torch.Tensor], norm_w: torch.Tensor, eps: float,
-               w: torch.Tensor, h_out: torch.Tensor, swiglu: bool = False, gemv: bool = True):
-    """The decode layer's residual add + RMSNorm and the projection of its
-    output, on (B, 1, K) rows: returns (h, y) with h = h + delta written to
-    h_out (h itself when delta is None) — one tg_gemv_rmsnorm launch where
-    the GEMV serves the projection, else add_rmsnorm and _proj."""
-    B, _, Kd = h.shape
-    if _FUSE_NORM and _gemv_serves(B, Kd, w.shape[0], gemv):
-        hn, y = ops.gemv_rmsnorm(h.view(B, Kd), None if delta is None else delta.view(B, Kd), norm_w, eps, w,
-                                 swiglu=swiglu, h_out=None if delta is None else h_out.view(B, Kd))
-        return (h if delta is None else h_out), y.view(B, 1, -1)
-    hn, x = ops.add_rmsnorm(h, delta, norm_w, eps, h_out=h_out if delta is not None else None)
-    return hn, _proj(x, w, swiglu=swiglu, gemv=gemv)
 
 
 class _DecodeCache:
@@ -184,29 +160,15 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
         lg_buf = torch.empty((B, model.lm_head.weight.shape[0]), dtype=torch.float32, device=device)
         extra = max_new_tokens - 1
 
-        # the residual stream alternates between two rows buffers (the fused
-        # norm + projection reads h in every CTA while one writes h + delta)
-        hbufs = [torch.empty((B, 1, inner.embed_tokens.weight.shape[1]), dtype=torch.bfloat16, device=device)
-                 for _ in range(2)]
-
         def step_body():
             h = inner.embed_tokens(cur)                                               # (B, 1, H)
             cos, sin = inner.rotary_emb(h, pos)
             delta = None
-            flip = 0
-
-            def norm_proj(h, delta, norm_w, eps, w, swiglu=False):
-                nonlocal flip
-                hn, y = _norm_proj(h, delta, norm_w, eps, w, hbufs[flip], swiglu=swiglu, gemv=use_gemv)
-                if delta is not None:
-                    flip ^= 1
-                return hn, y
-
             for i in range(n_layers):
                 lw = fw[i]
                 below = i <= gate_layer
-                h, qkv = norm_proj(h, delta, lw.in_w, lw.eps, lw.wqkv)
-                qkv = qkv.view(B, 1, nq + 2 * nkv, D)
+                h, x = ops.add_rmsnorm(h, delta, lw.in_w, lw.eps, h_out=h if delta is not None else None)
+                qkv = _proj(x, lw.wqkv, gemv=use_gemv).view(B, 1, nq + 2 * nkv, D)
                 q = qkv[:, :, :nq]
                 k = qkv[:, :, nq:nq + nkv]
                 v = qkv[:, :, nq + nkv:]
@@ -222,10 +184,10 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
                                              bias=bias[li], q_scale=qs_cur[li] if qs_cur is not None else None,
                                              n_keys_dev=nk_2)
                 o = _proj(a.view(B, 1, nq * D), lw.wo, gemv=use_gemv)
-                h, act = norm_proj(h, o, lw.post_w, lw.eps, lw.wgu, swiglu=True)
-                delta = _proj(act, lw.wdown, gemv=use_gemv)
-            _, lg = norm_proj(h, delta, inner.norm.weight, float(inner.norm.variance_epsilon), model.lm_head.weight)
-            lg = lg[:, -1]
+                h, x2 = ops.add_rmsnorm(h, o, lw.post_w, lw.eps, h_out=h)
+                delta = _proj(_proj(x2, lw.wgu, swiglu=True, gemv=use_gemv), lw.wdown, gemv=use_gemv)
+            _, hn = ops.add_rmsnorm(h, delta, inner.norm.weight, float(inner.norm.variance_epsilon))
+            lg = _proj(hn, model.lm_head.weight, gemv=use_gemv)[:, -1]
             lg_buf.copy_(lg)
             cur.copy_(lg.argmax(-1, keepdim=True))
             pos.add_(1)

@@ -585,44 +585,6 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_valid:
 
 
 # ----------------------------------------------------------------- decode projections
-def gemv_rmsnorm(h: torch.Tensor, delta: Optional[torch.Tensor], norm_w: torch.Tensor, eps: float, w: torch.Tensor,
-                 swiglu: bool = False, h_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None):
-    """add_rmsnorm(h, delta, norm_w, eps) then gemv of its x, one launch
-    (tg_gemv_rmsnorm): h, delta (B, K) bf16 rows; returns (h_out, y) with
-    h_out = bf16(h + delta) (h itself when delta is None) and y the gemv of
-    the RMSNorm of h_out, bit-identical to the two ops. h_out must not be h
-    or delta (allocated when None)."""
-    _require_cuda("h", h, torch.bfloat16)
-    _require_cuda("norm_w", norm_w, torch.bfloat16)
-    _require_cuda("w", w, torch.bfloat16)
-    if h.dim() != 2 or h.stride(1) != 1 or w.dim() != 2 or w.stride(1) != 1 or h.shape[1] != w.shape[1]:
-        raise ValueError(f"h {tuple(h.shape)} (B, K) and w {tuple(w.shape)} (N, K) with contiguous rows")
-    B, K = h.shape
-    d_ptr, d_ld, ho_ptr, ho_ld = None, 0, None, 0
-    if delta is not None:
-        _require_cuda("delta", delta, torch.bfloat16)
-        if delta.shape != h.shape or delta.stride(1) != 1:
-            raise ValueError("delta must match h")
-        if h_out is None:
-            h_out = torch.empty_like(h)
-        if h_out.shape != h.shape or h_out.stride(1) != 1:
-            raise ValueError("h_out must match h")
-        d_ptr, d_ld, ho_ptr, ho_ld = delta.data_ptr(), delta.stride(0), h_out.data_ptr(), h_out.stride(0)
-    else:
-        h_out = h
-    N = w.shape[0] // 2 if swiglu else w.shape[0]
-    if swiglu and w.shape[0] % 2:
-        raise ValueError("the fused [gate; up] weight has an even number of rows")
-    if out is None:
-        out = torch.empty((B, N), dtype=torch.bfloat16, device=h.device)
-    L = _lib.lib()
-    with _device_ctx(h):
-        _lib.check(L.tg_gemv_rmsnorm(h.data_ptr(), h.stride(0), d_ptr, d_ld, ho_ptr, ho_ld, norm_w.data_ptr(),
-                                     float(eps), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
-                                     B, N, K, int(bool(swiglu)), _stream(h)))
-    return h_out, out
-
-
 def gemv(x: torch.Tensor, w: torch.Tensor, swiglu: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x @ w.T for the decode step's few rows (tg_gemv): x (B, K) bf16 with
     B <= 8 and K a multiple of 256, w (N, K) bf16 (row-major, contiguous
