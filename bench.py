@@ -16,9 +16,10 @@ Reported (one JSON line from rank 0):
   value        prefill tokens/s over all ranks, prompt ids already on the GPU,
                device time (CUDA events) of K steps, max over ranks;
   e2e          the same metric through the public API
-               (TokenGateModel.generate with host ids: the H2D copy of the ids
-               and the D2H read of the first token and kept positions inside
-               the timed region), wall clock with syncs, max over ranks;
+               (TokenGateModel.generate with the ids in pinned host memory:
+               the H2D copy of the ids and the D2H read of the first token and
+               kept positions inside the timed region), wall clock with
+               syncs, max over ranks;
   roofline     the key-bias attention kernel (the dominant kernel): its
                algorithmic FLOPs (4*B*Hq*D*S(S+1)/2 per causal launch) over its
                CUDA-event time on its launch stream during the timed steps,
@@ -57,6 +58,13 @@ GATE_LAYER = 1
 MODEL = "qwen3-1.7b"
 CPU_SAMPLE = dict(seq_len=8192, state_begin=512, state_end=7936, K=464)
 METRIC = "gated-prefill tokens/s (Qwen3-1.7B shape, 32k ctx, K=2000)"
+# DRAM traffic of one Phase-1 attention launch (B=1, S=32768, Hq=16, Hkv=8),
+# dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture of the
+# same launch shape (1.008 GB read + 0.112 GB written; algorithmic 0.256 +
+# 0.128 GB: K/V re-read by the row blocks that share them)
+ATTN_TRAFFIC_BYTES = 1.120e9
+ATTN_TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:keybias -s 3 -c 1 "
+                       "python -m tokengate_b200.microbench attn --seq 32768 --iters 3")
 
 
 def _dist():
@@ -309,8 +317,10 @@ def main():
         return tm.prefill([ids_dev], starts, ends, K_KEEP)[0]
 
     from tokengate_b200.inference import with_state_span
-    host_ids = with_state_span(prompt[:STATE_BEGIN].tolist(), prompt[STATE_BEGIN:STATE_END].tolist(),
-                               prompt[STATE_END:].tolist())
+    # one request's ids (state-span sentinels included) in pinned host
+    # memory, as a serving front end hands them over; copied every step
+    host_ids = torch.tensor(with_state_span(prompt[:STATE_BEGIN].tolist(), prompt[STATE_BEGIN:STATE_END].tolist(),
+                                            prompt[STATE_END:].tolist()), dtype=torch.long).pin_memory()
 
     def step_e2e():
         return tm.generate(host_ids, None, max_kept_prefill_tokens=K_KEEP)
@@ -378,7 +388,7 @@ def main():
     barrier()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e_value = world * SEQ_LEN * args.steps / e2e_s
-    h2d = SEQ_LEN * 8
+    h2d = host_ids.numel() * 8
     d2h = 8 + out.n_kept[0] * 8
 
     peaks = _peaks()
@@ -404,7 +414,8 @@ def main():
                      "frac": (achieved / peaks["tflops"]) if achieved else None,
                      "peak_source": f"{peaks['source']} bf16 sustained",
                      "launches": a_n, "algorithmic_tflop": a_flops / 1e12, "kernel_ms": a_ms,
-                     "traffic": None},
+                     "traffic": ATTN_TRAFFIC_BYTES, "traffic_unit": "bytes per launch",
+                     "traffic_source": ATTN_TRAFFIC_SOURCE},
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu_baseline:   # rank 0 at N=1 only

@@ -188,6 +188,27 @@ def test_generate_api(tiny, cuda):
         tm.generate(list(range(10)), None)
 
 
+def test_generate_tensor_ids_match_list_ids(tiny, cuda):
+    """generate on the ids as a Python list, a pinned host tensor (scanned
+    through a zero-copy view, copied whole and cut on the device) and a CUDA
+    tensor: the same kept positions and first tokens; a tensor without a
+    valid state span is rejected as the list is."""
+    model, gate = tiny["model"], tiny["gate"]
+    tm = TokenGateModel(model, gate, 1, "tiny")
+    g = torch.Generator().manual_seed(41)
+    ids = with_state_span(torch.randint(0, 1000, (6,), generator=g).tolist(),
+                          torch.randint(0, 1000, (290,), generator=g).tolist(),
+                          torch.randint(0, 1000, (9,), generator=g).tolist())
+    ref = tm.generate(ids, None, max_kept_prefill_tokens=30)
+    pinned = torch.tensor(ids, dtype=torch.long).pin_memory()
+    for t in (pinned, torch.tensor(ids, dtype=torch.int32), pinned.to(cuda)):
+        got = tm.generate(t, None, max_kept_prefill_tokens=30)
+        assert got.n_kept == ref.n_kept and got.n_state == ref.n_state
+        assert got.kept_pos == ref.kept_pos and got.token_ids == ref.token_ids
+    with pytest.raises(ValueError):
+        tm.generate(torch.arange(10).pin_memory(), None)
+
+
 def test_load_model_synthetic(cuda):
     small = dict(hidden_size=256, intermediate_size=512, num_hidden_layers=3, num_attention_heads=2,
                  num_key_value_heads=1, head_dim=128, vocab_size=500, rope_theta=1e6)

@@ -49,12 +49,20 @@ def split_state_span(ids: List[int]):
     return clean, s, e - 1
 
 
-def _split_state_span_tensor(ids):
+def _split_state_span_tensor(ids, device=None):
     """split_state_span for the generate path: one conversion of the ids to an
     int64 array (a list of Python ints costs ~30 ns per id to convert; the
     sentinel scan and the cut are vectorized), the clean ids returned as a CPU
-    int64 tensor. Same checks and error as split_state_span."""
-    a = ids.cpu().numpy() if torch.is_tensor(ids) else np.asarray(ids, dtype=np.int64)
+    int64 tensor. A CPU tensor of ids (pinned, for one asynchronous copy) is
+    scanned through a zero-copy view and, when `device` is a CUDA device,
+    copied whole and cut on that device. Same checks and error as
+    split_state_span."""
+    host = None
+    if torch.is_tensor(ids):
+        host = ids if ids.device.type == "cpu" else ids.cpu()
+        a = host.numpy()
+    else:
+        a = np.asarray(ids, dtype=np.int64)
     if a.ndim != 1:
         raise ValueError(f"ids must be one flat sequence per prompt, got shape {a.shape}")
     ss = np.flatnonzero(a == STATE_START_ID)
@@ -65,6 +73,10 @@ def _split_state_span_tensor(ids):
             f"STATE_END_ID (produce ids with apply_chat_template(state=...)); found starts={ss.tolist()} "
             f"ends={ee.tolist()}")
     s, e = int(ss[0]), int(ee[0])
+    if host is not None and device is not None and torch.device(device).type == "cuda":
+        d = ids if ids.device == torch.device(device) else host.to(device, non_blocking=True)
+        d = d.to(torch.long)
+        return torch.cat((d[:s], d[s + 1:e], d[e + 1:])), s, e - 1
     clean = np.concatenate((a[:s], a[s + 1:e], a[e + 1:])).astype(np.int64, copy=False)
     return torch.from_numpy(clean), s, e - 1
 
@@ -122,12 +134,12 @@ class TokenGateModel:
             ids = [ids] if ids.ndim == 1 else list(ids)
         elif len(ids) and isinstance(ids[0], (int, np.integer)):
             ids = [ids]
-        split = [_split_state_span_tensor(seq) for seq in ids]
+        dev = next(self.model.parameters()).device
+        split = [_split_state_span_tensor(seq, dev) for seq in ids]
         clean = [s[0] for s in split]
         starts = [s[1] for s in split]
         ends = [s[2] for s in split]
         k = _NO_PRUNING if max_kept_prefill_tokens is None else max_kept_prefill_tokens
-        dev = next(self.model.parameters()).device
         if max_new_tokens > 1:
             # gated prefill + greedy decode over the gated KV cache (decode.generate_batch)
             from .decode import generate_batch
