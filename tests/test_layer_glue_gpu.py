@@ -111,11 +111,13 @@ def test_qk_norm_rope_append(cuda):
     assert torch.equal(kc[:, others], kc0[:, others]) and torch.equal(vc[:, others], vc0[:, others])
 
 
-def test_silu_mul(cuda):
+@pytest.mark.parametrize("inter", [6144, 2400, 8])
+def test_silu_mul(cuda, inter):
+    # 2400: 300 vectors per row, a partial second pass of the per-row loop
     g = torch.Generator(device=cuda).manual_seed(2)
-    gu = (torch.randn(5, 77, 2 * 6144, device=cuda, generator=g) * 3).to(torch.bfloat16)
+    gu = (torch.randn(5, 77, 2 * inter, device=cuda, generator=g) * 3).to(torch.bfloat16)
     out = ops.silu_mul(gu)
-    ref = F.silu(gu[..., :6144]) * gu[..., 6144:]
+    ref = F.silu(gu[..., :inter]) * gu[..., inter:]
     _close_bf16(out, ref, min_exact=0.98)
 
 

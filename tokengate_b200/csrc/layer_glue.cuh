@@ -306,31 +306,48 @@ struct SiluParams {
   int64_t ld_gu, ld_out;
 };
 
+// One block per row at a time (grid-stride over rows), threads across the
+// row's 16-byte vectors, up to kSiluUnroll vectors of gate and up loaded per
+// thread before any arithmetic; no integer division per vector.
+constexpr int kSiluUnroll = 4;
+
 __global__ void __launch_bounds__(256) silu_mul_kernel(const SiluParams p) {
   griddep_wait();  // launched with programmatic stream serialization
   griddep_launch_dependents();
-  const int64_t vec_per_row = p.inter >> 3;
-  const int64_t total = p.rows * vec_per_row;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += stride) {
-    const int64_t row = v / vec_per_row;
-    const int64_t c = v - row * vec_per_row;
-    const uint4* gp = reinterpret_cast<const uint4*>(p.gu + row * p.ld_gu) + c;
-    const uint4 g4 = ld_nc_v4(gp);
-    const uint4 u4 = ld_nc_v4(gp + vec_per_row);
-    const uint32_t* g = reinterpret_cast<const uint32_t*>(&g4);
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(&u4);
-    uint4 o4;
-    uint32_t* o = reinterpret_cast<uint32_t*>(&o4);
+  const int vpr = (int)(p.inter >> 3);
+  for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const uint4* gp = reinterpret_cast<const uint4*>(p.gu + row * p.ld_gu);
+    uint4* op = reinterpret_cast<uint4*>(p.out + row * p.ld_out);
+    for (int c0 = threadIdx.x; c0 < vpr; c0 += kSiluUnroll * 256) {
+      uint4 g4[kSiluUnroll], u4[kSiluUnroll];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float g0 = bf16_lo(g[e]), g1 = bf16_hi(g[e]);
-      float a0 = g0 / (1.f + expf(-g0));
-      float a1 = g1 / (1.f + expf(-g1));
-      round_bf16x2(a0, a1);
-      o[e] = pack_bf16x2(a0 * bf16_lo(u[e]), a1 * bf16_hi(u[e]));
+      for (int j = 0; j < kSiluUnroll; ++j) {
+        const int c = c0 + j * 256;
+        if (c < vpr) {
+          g4[j] = ld_nc_v4(gp + c);
+          u4[j] = ld_nc_v4(gp + vpr + c);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kSiluUnroll; ++j) {
+        const int c = c0 + j * 256;
+        if (c < vpr) {
+          const uint32_t* g = reinterpret_cast<const uint32_t*>(&g4[j]);
+          const uint32_t* u = reinterpret_cast<const uint32_t*>(&u4[j]);
+          uint4 o4;
+          uint32_t* o = reinterpret_cast<uint32_t*>(&o4);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float g0 = bf16_lo(g[e]), g1 = bf16_hi(g[e]);
+            float a0 = g0 / (1.f + expf(-g0));
+            float a1 = g1 / (1.f + expf(-g1));
+            round_bf16x2(a0, a1);
+            o[e] = pack_bf16x2(a0 * bf16_lo(u[e]), a1 * bf16_hi(u[e]));
+          }
+          op[c] = o4;
+        }
+      }
     }
-    reinterpret_cast<uint4*>(p.out + row * p.ld_out)[c] = o4;
   }
 }
 

@@ -627,7 +627,8 @@ int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_
   p.inter = inter;
   p.ld_gu = ld_gu;
   p.ld_out = ld_out;
-  const int64_t blocks = resident_blocks((rows * (inter / 8) + 255) / 256, 8);
+  if (inter / 8 > (int64_t)INT32_MAX) return fail(TG_ERR_UNSUPPORTED, "silu_mul: inter %lld", (long long)inter);
+  const int64_t blocks = resident_blocks(rows, 8);   // a block per row at a time
   cudaError_t e = launch_pdl(tg::silu_mul_kernel, dim3((unsigned)blocks), dim3(256), 0,
                              static_cast<cudaStream_t>(stream), p);
   if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");

@@ -8,6 +8,7 @@
     python -m tokengate_b200.microbench tables [--k 2000] [--layers 26] [--hq 16] [--batch 1]
     python -m tokengate_b200.microbench decode [--seq 2768] [--batch 1] [--hq 16] [--hkv 8] [--no-bias]
     python -m tokengate_b200.microbench gemv [--n 12288] [--hidden 2048] [--batch 1]
+    python -m tokengate_b200.microbench gemvchain [--layers 26] [--hidden 2048] [--inter 6144] [--batch 1]
     python -m tokengate_b200.microbench generate [--seq 32768] [--k 2000] [--batch 1] [--new 64] [--gate linear|e2e] [--proj gemv|cublas]
 
 Prints one JSON line per run with the CUDA-event time per launch and the
@@ -69,7 +70,7 @@ def _graph_time(fn, n, reps, warmup=3):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=("attn", "score", "topk", "gather", "branch", "tables", "decode",
-                                       "generate", "gemv"))
+                                       "generate", "gemv", "gemvchain"))
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--new", type=int, default=64)
     ap.add_argument("--gate", default="linear", choices=("linear", "e2e"))
@@ -112,6 +113,34 @@ def main(argv=None):
         byts = a.n * a.hidden * 2 + B * (a.hidden + a.n) * 2
         res.update(n=a.n, k=a.hidden, ms=ms, us=ms * 1e3, mbytes=byts / 1e6, gbs=byts / ms / 1e6,
                    cublas_us=ms_ref * 1e3, cublas_gbs=byts / ms_ref / 1e6)
+    elif a.kernel == "gemvchain":
+        # the decode step's layer projections alone: per layer q/k/v, o,
+        # gate/up (+SwiGLU) and down GEMVs chained through their outputs, over
+        # --layers + 2 layers of distinct weights (not L2-resident), one
+        # CUDA graph; then the four kernels on one layer's (L2-resident)
+        # weights, the per-layer latency floor of the chain
+        H, I, NQ, NL = a.hidden, a.inter, 2 * a.hidden, a.layers + 2
+        mk = lambda n, k: (torch.randn(n, k, device=dev, generator=g) / k ** 0.5).to(torch.bfloat16)
+        W = [(mk(NQ, H), mk(H, H), mk(2 * I, H), mk(H, I)) for _ in range(NL)]
+        x = torch.randn(B, H, device=dev, dtype=torch.bfloat16, generator=g)
+        yq = torch.empty(B, NQ, device=dev, dtype=torch.bfloat16)
+        yo = torch.empty(B, H, device=dev, dtype=torch.bfloat16)
+        act = torch.empty(B, I, device=dev, dtype=torch.bfloat16)
+
+        def layer(w):
+            ops.gemv(x, w[0], out=yq)
+            ops.gemv(yq[:, :H], w[1], out=yo)
+            ops.gemv(yo, w[2], swiglu=True, out=act)
+            ops.gemv(act, w[3], out=x)
+
+        def chain():
+            for w in W:
+                layer(w)
+        ms = _graph_time(chain, 1, a.iters)
+        ms_l2 = _graph_time(lambda: layer(W[0]), NL, a.iters)
+        byts = NL * sum(t.numel() for t in W[0]) * 2
+        res.update(layers=NL, hidden=H, inter=I, ms=ms, us_per_layer=ms * 1e3 / NL, mbytes=byts / 1e6,
+                   gbs=byts / ms / 1e6, l2_resident_us_per_layer=ms_l2 * 1e3)
     elif a.kernel == "generate":
         from .decode import generate_batch
         from .inference import load_model
