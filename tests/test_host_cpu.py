@@ -3,6 +3,7 @@ import ctypes
 import os
 import re
 
+import numpy as np
 import pytest
 import torch
 
@@ -111,6 +112,23 @@ def test_state_span():
                 [STATE_START_ID, 1, STATE_END_ID, STATE_END_ID]):
         with pytest.raises(ValueError):
             split_state_span(bad)
+
+
+def test_state_span_tensor_inputs():
+    """The generate path's splitter takes a list, an int64 / int32 CPU tensor
+    or a numpy array; on CPU (no CUDA device given) every form gives the
+    list's clean ids and span, and invalid spans raise for tensors too."""
+    from tokengate_b200.inference import _split_state_span_tensor
+    ids = with_state_span([1, 2], [10, 11, 12], [3])
+    want = ([1, 2, 10, 11, 12, 3], 2, 5)
+    for form in (ids, torch.tensor(ids), torch.tensor(ids, dtype=torch.int32), np.asarray(ids)):
+        clean, s, e = _split_state_span_tensor(form)
+        assert (clean.tolist(), s, e) == want
+        clean, s, e = _split_state_span_tensor(form, torch.device("cpu"))
+        assert (clean.tolist(), s, e) == want
+    for bad in ([1, 2, 3], [STATE_END_ID, 1, STATE_START_ID]):
+        with pytest.raises(ValueError):
+            _split_state_span_tensor(torch.tensor(bad))
 
 
 def test_bias_layouts():
