@@ -223,3 +223,16 @@ def test_gemv_vs_cublas(cuda, B, N, K):
         ref_act = ops.silu_mul(torch.nn.functional.linear(x, w)).float()
         assert ((act - ref_act).abs() <= 2 ** -6 * ref_act.abs() + 2e-3).all()
         assert (act == ref_act).float().mean().item() >= 0.9
+
+
+def test_rotary_table_equals_per_step(tiny, cuda):
+    """The decode step gathers its rotary cos / sin from a table the model's
+    rotary embedding makes for all decode positions at once; that table is
+    bit-identical to making each position's row on its own step."""
+    inner = tiny["model"].model
+    like = torch.empty((2, 1, 1), dtype=inner.embed_tokens.weight.dtype, device=cuda)
+    pos = torch.tensor([[301], [4093]], device=cuda) + torch.arange(9, device=cuda).view(1, 9)
+    cos_t, sin_t = inner.rotary_emb(like, pos)
+    for s in range(9):
+        c, si = inner.rotary_emb(like, pos[:, s:s + 1])
+        assert torch.equal(c, cos_t[:, s:s + 1]) and torch.equal(si, sin_t[:, s:s + 1])

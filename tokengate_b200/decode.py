@@ -150,19 +150,28 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
         # step state on the device, so that one captured step serves every
         # step: the token, its position, each cache's append slot and key count
         cur = first.clone()
-        pos = next_pos.view(B, 1).clone()
         wb, w2 = dc.width[0], dc.width[n_layers - 1]
-        slot_b = torch.tensor([wb], dtype=torch.int64, device=device)
-        slot_2 = torch.tensor([w2], dtype=torch.int64, device=device)
-        nk_b = torch.tensor([wb + 1], dtype=torch.int32, device=device)
-        nk_2 = torch.tensor([w2 + 1], dtype=torch.int32, device=device)
+        extra = max_new_tokens - 1
+        # the counters one step advances, one add each: the two caches' append
+        # slots and the step index (int64), the two key counts (int32)
+        ctr = torch.tensor([wb, w2, 0], dtype=torch.int64, device=device)
+        slot_b, slot_2, step_idx = ctr[0:1], ctr[1:2], ctr[2:3]
+        nkc = torch.tensor([wb + 1, w2 + 1], dtype=torch.int32, device=device)
+        nk_b, nk_2 = nkc[0:1], nkc[1:2]
+        # the rotary cos / sin of every decode position, made once by the
+        # model's own rotary embedding (elementwise in the position, so equal
+        # to making them step by step); a step gathers its row
+        step_pos = next_pos.view(B, 1) + torch.arange(extra, device=device).view(1, extra)      # (B, extra)
+        like = torch.empty((B, 1, 1), dtype=inner.embed_tokens.weight.dtype, device=device)
+        cos_t, sin_t = inner.rotary_emb(like, step_pos)
+        rot = torch.stack((cos_t, sin_t), dim=2)                                                 # (B, extra, 2, D)
         qs_cur = torch.empty_like(qs_all[0]) if qs_all is not None else None
         lg_buf = torch.empty((B, model.lm_head.weight.shape[0]), dtype=torch.float32, device=device)
-        extra = max_new_tokens - 1
 
         def step_body():
             h = inner.embed_tokens(cur)                                               # (B, 1, H)
-            cos, sin = inner.rotary_emb(h, pos)
+            r = rot.index_select(1, step_idx)                                         # (B, 1, 2, D)
+            cos, sin = r[:, :, 0], r[:, :, 1]
             delta = None
             for i in range(n_layers):
                 lw = fw[i]
@@ -190,9 +199,8 @@ def generate_batch(model, gate, prompt_ids_list: Sequence, article_starts: Seque
             lg = _proj(hn, model.lm_head.weight, gemv=use_gemv)[:, -1]
             lg_buf.copy_(lg)
             cur.copy_(lg.argmax(-1, keepdim=True))
-            pos.add_(1)
-            for t_ in (slot_b, slot_2, nk_b, nk_2):
-                t_.add_(1)
+            ctr.add_(1)
+            nkc.add_(1)
 
         graph = None
         eos_seen = torch.zeros(B, dtype=torch.bool, device=device)
