@@ -48,7 +48,7 @@ const char* tg_last_error(void);
 int tg_device_error(void* stream, unsigned int* flags_out, int clear);
 
 /*
- * a1 — causal GQA attention with an additive per-key bias, forward.
+ * Causal GQA attention with an additive per-key bias, forward.
  *
  * Replaces the reference key-bias operator
  *   torch.ops.recursive_kvs.fa2_keybias_fwd(q, k, v, bias_raw, scale, causal)
@@ -89,7 +89,7 @@ int tg_keybias_attn_fwd(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
                         float softmax_scale, int causal, void* stream);
 
 /*
- * a4 — gate scorer: score[b, r] = logsigmoid( sum_e float(h[b, row_begin[b]+r, e]) * w[e] )
+ * Gate scorer: score[b, r] = logsigmoid( sum_e float(h[b, row_begin[b]+r, e]) * w[e] )
  * for r < row_count[b].
  *
  * Replaces the synthetic linear gate's scoring of the state span,
@@ -109,7 +109,7 @@ int tg_gate_score(const void* hidden, int64_t h_sb, int64_t h_ss, int hidden_dim
                   float* scores, int64_t s_sb, void* stream);
 
 /*
- * a6 + a7 (positions, bias) — top-K selection and the kept-position list.
+ * Top-K selection and the kept-position list.
  *
  * Replaces, per request b, the selection and keep-list construction
  *   K_clamped = max(1, min(K, n_art)); topk = torch.topk(score, K_clamped)
@@ -139,7 +139,7 @@ int tg_topk_select(const float* scores, int64_t s_sb, int B, const int32_t* n_st
                    int bias_dtype, int64_t* topk_local, int64_t tl_sb, void* stream);
 
 /*
- * a7 / a8 — compaction: gather kept rows of several tensors in one launch.
+ * Compaction: gather kept rows of several tensors in one launch.
  *
  * Replaces hs_pruned[b, :n] = hidden_states[b, keep]
  *   (tokengate/e2e_gate/gate_module/gate_forward.py:1443-1461)
@@ -175,7 +175,7 @@ int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t
                    int64_t idx_sb, int B, int n_rows, const int32_t* n_valid, void* stream);
 
 /*
- * Decoder-layer glue (SURVEY next row: fused prologues). Each replaces an
+ * Decoder-layer glue (the fused layer prologues). Each replaces an
  * eager op chain of the transformers Qwen3 layer that the reference runs
  * around its patched attention (tokengate/e2e_gate/attn/qwen3_flex_attention.py:
  * 539-551 q/k projections + q_norm/k_norm + apply_rotary_pos_emb, :646-648
@@ -241,7 +241,7 @@ int tg_branch_score(const void* gu, int64_t gu_sb, int64_t gu_ss, int inter, con
                     int64_t s_sb, void* stream);
 
 /*
- * a5 + a9 + a2 (finalized gate) — the Phase-2 operands of every biased layer
+ * The finalized gate's Phase-2 operands of every biased layer
  * from the raw branch scores, in one launch. For request b, kept slot t
  * (position p = keep[b, t]), Phase-2 layer l and head h:
  *   rs      = rsqrt(mean over the state span of score^2 + eps)
@@ -274,7 +274,7 @@ int tg_phase2_tables(const float* scores, int64_t s_sb, int B, const int32_t* st
                      float* bias, float* q_scale, void* stream);
 
 /*
- * f4 — decode attention (the decode side of the gated generation): one
+ * Decode attention (the decode side of the gated generation): one
  * query token per (batch row, head) against the gated KV cache.
  *
  * Replaces the decode step's attention of the reference's gated generation,
@@ -321,7 +321,7 @@ int tg_decode_attn_ex(const void* q, int64_t q_sb, int64_t q_sh,
                       void* workspace, size_t workspace_bytes,
                       int B, int Hq, int Hkv, int D, float softmax_scale, void* stream);
 
-/* f4 — decode projections: y[b, :] = x[b, :] W^T for B <= 8 rows (the
+/* Decode projections: y[b, :] = x[b, :] W^T for B <= 8 rows (the
  * decode step's tokens), x (B, K) bf16 row stride ld_x, W (N, K) bf16
  * row-major row stride ld_w, y (B, N) bf16 row stride ld_y; K a multiple of
  * 256; x and W 16-byte aligned with row strides multiples of 8. With swiglu

@@ -1,4 +1,4 @@
-"""Fused Qwen3 decoder layer for the gated prefill (SURVEY next row: fused prologues).
+"""Fused Qwen3 decoder layer for the gated prefill: the layer prologues and glue as fused kernels.
 
 The transformers Qwen3DecoderLayer the reference runs (with its attention
 patched, tokengate/e2e_gate/attn/qwen3_flex_attention.py:475-652) issues ~30
