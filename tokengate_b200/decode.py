@@ -63,10 +63,16 @@ def _proj(x: torch.Tensor, w: torch.Tensor, swiglu: bool = False, gemv: bool = T
     tensor cores beyond that, first on the 151936-row lm_head), cuBLAS
     otherwise or when gemv is False."""
     B, _, Kd = x.shape
-    if gemv and Kd % 256 == 0 and (B <= 2 or (B <= 4 and w.shape[0] < 32768)):
+    if gemv and Kd % 256 == 0 and (B <= 2 or (B <= _GEMV_LAYER_MAX_B and w.shape[0] < 32768)):
         return ops.gemv(x.view(B, Kd), w, swiglu=swiglu).view(B, 1, -1)
     y = F.linear(x, w)
     return ops.silu_mul(y) if swiglu else y
+
+
+# the largest batch whose layer projections (fewer than 32768 output rows)
+# run on tg_gemv (measured on B200: at B = 6 and 8 the decode step is
+# 8-15 % slower with them there than on cuBLAS)
+_GEMV_LAYER_MAX_B = 4
 
 
 class _DecodeCache:
