@@ -47,19 +47,25 @@ __device__ __forceinline__ float gemv_silu(float g) {
 // two passes into L2 (a hint only: the rows are loaded after the wait).
 constexpr int kGemvBatch = 8;
 
-template <int R>
-__device__ __forceinline__ void gemv_load_batch(uint4 (&wv)[R][kGemvBatch], const __nv_bfloat16* w,
-                                                const GemvParams& p, int64_t n, int s0, int n_slices, int lane) {
+// A whole long row in one batch for the plain form with few rows (K up to
+// 6144: 24 slices), where a row per warp in 8-slice batches leaves the
+// launch bound by the latency of dependent loads.
+constexpr int kGemvLongBatch = 24;
+
+template <int R, int NB>
+__device__ __forceinline__ void gemv_load_batch(uint4 (&wv)[R][NB], const __nv_bfloat16* w, const GemvParams& p,
+                                                int64_t n, int s0, int n_slices, int lane) {
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const uint4* row = reinterpret_cast<const uint4*>(w + (n + r * p.N) * p.ld_w + 8 * lane) + 32 * s0;
 #pragma unroll
-    for (int u = 0; u < kGemvBatch; ++u)
+    for (int u = 0; u < NB; ++u)
       if (s0 + u < n_slices) wv[r][u] = ld_nc_v4(row + 32 * u);
   }
 }
 
-template <int BT, bool kSwiGlu>
+// NB: 512-byte slices per batch (kGemvBatch, or kGemvLongBatch).
+template <int BT, bool kSwiGlu, int NB = kGemvBatch>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(16) uint8_t gsm[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(gsm);  // [BT][K]
@@ -76,8 +82,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
   griddep_wait();
   const __nv_bfloat16* x = p.x;
   const __nv_bfloat16* w = p.w;
-  uint4 wv[R][kGemvBatch];
-  if (warp_global < p.N) gemv_load_batch<R>(wv, w, p, warp_global, 0, n_slices, lane);
+  uint4 wv[R][NB];
+  if (warp_global < p.N) gemv_load_batch<R, NB>(wv, w, p, warp_global, 0, n_slices, lane);
   // x rows into shared memory (rows past B are zero)
   for (int i = t; i < BT * (K / 8); i += kGemvThreads) {
     const int b = i / (K / 8), c = i - b * (K / 8);
@@ -94,9 +100,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
     for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int b = 0; b < BT; ++b) acc[r][b] = 0.f;
-    for (int s0 = 0; s0 < n_slices; s0 += kGemvBatch) {
+    for (int s0 = 0; s0 < n_slices; s0 += NB) {
 #pragma unroll
-      for (int u = 0; u < kGemvBatch; ++u) {
+      for (int u = 0; u < NB; ++u) {
         if (s0 + u < n_slices) {
 #pragma unroll
           for (int b = 0; b < BT; ++b) {
@@ -116,10 +122,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
         }
       }
       // the next batch: the rest of this row, else the first of the next
-      if (s0 + kGemvBatch < n_slices)
-        gemv_load_batch<R>(wv, w, p, n, s0 + kGemvBatch, n_slices, lane);
+      if (s0 + NB < n_slices)
+        gemv_load_batch<R, NB>(wv, w, p, n, s0 + NB, n_slices, lane);
       else if (n + n_warps < p.N)
-        gemv_load_batch<R>(wv, w, p, n + n_warps, 0, n_slices, lane);
+        gemv_load_batch<R, NB>(wv, w, p, n + n_warps, 0, n_slices, lane);
     }
 #pragma unroll
     for (int r = 0; r < R; ++r)

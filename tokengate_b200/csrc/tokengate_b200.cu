@@ -159,14 +159,14 @@ constexpr int kGemvMaxSmem = 200 * 1024;  // the rows of x in shared memory: BT 
 // One gemv launch: the kernel's shared-memory limit is raised once per device
 // (not per launch, so launches inside a stream capture issue no attribute
 // calls); two CTAs of 8 warps per SM, or fewer when there are fewer rows.
-template <int BT, bool SW>
-cudaError_t launch_gemv(const tg::GemvParams& p, cudaStream_t s, int dev) {
+template <int BT, bool SW, int NB>
+cudaError_t launch_gemv_nb(const tg::GemvParams& p, cudaStream_t s, int dev) {
   static bool attr_set[kMaxDevices] = {};
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(tg::gemv_kernel<BT, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kGemvMaxSmem);
+      cudaError_t e = cudaFuncSetAttribute(tg::gemv_kernel<BT, SW, NB>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem);
       if (e != cudaSuccess) return e;
       attr_set[dev] = true;
     }
@@ -174,7 +174,19 @@ cudaError_t launch_gemv(const tg::GemvParams& p, cudaStream_t s, int dev) {
   const int smem = BT * p.K * 2;
   const int64_t groups = (p.N + tg::kGemvWarps - 1) / tg::kGemvWarps;
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(groups, 2LL * sm_count()));
-  return launch_pdl(tg::gemv_kernel<BT, SW>, dim3((unsigned)blocks), dim3(tg::kGemvThreads), (size_t)smem, s, p);
+  return launch_pdl(tg::gemv_kernel<BT, SW, NB>, dim3((unsigned)blocks), dim3(tg::kGemvThreads), (size_t)smem, s,
+                    p);
+}
+
+// the plain form with at most 4 rows and K of 16 slices or more loads a
+// whole row per batch; everything else 8 slices
+template <int BT, bool SW>
+cudaError_t launch_gemv(const tg::GemvParams& p, cudaStream_t s, int dev) {
+  if constexpr (!SW && BT <= 4) {
+    if (p.K / 256 >= 16 && p.K / 256 <= tg::kGemvLongBatch)
+      return launch_gemv_nb<BT, SW, tg::kGemvLongBatch>(p, s, dev);
+  }
+  return launch_gemv_nb<BT, SW, tg::kGemvBatch>(p, s, dev);
 }
 }  // namespace
 
