@@ -54,10 +54,12 @@ def test_add_rmsnorm(cuda, H):
     assert none is None and torch.equal(h3, ref_h)
 
 
-def test_qk_norm_rope(cuda):
+@pytest.mark.parametrize("S", [300, 20])
+def test_qk_norm_rope(cuda, S):
+    # S = 20: 40 rows, the few-row launch that spreads a row's heads over warps
     from transformers.models.qwen3.configuration_qwen3 import Qwen3Config
     from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
-    B, S, nq, nkv, D = 2, 300, 16, 8, 128
+    B, nq, nkv, D = 2, 16, 8, 128
     g = torch.Generator(device=cuda).manual_seed(1)
     qkv = torch.randn(B, S, nq + 2 * nkv, D, device=cuda, generator=g).to(torch.bfloat16)
     qn = Qwen3RMSNorm(D, eps=1e-6).to(cuda).to(torch.bfloat16)
@@ -83,6 +85,25 @@ def test_qk_norm_rope(cuda):
     q2, k2 = qkv[:, :, :nq].contiguous(), qkv[:, :, nq:nq + nkv].contiguous()
     ops.qk_norm_rope(q2, k2, qn.weight, kn.weight, cos, sin, 1e-6)
     assert torch.equal(q2, got[:, :, :nq]) and torch.equal(k2, got[:, :, nq:nq + nkv])
+
+
+def test_qk_norm_rope_few_rows_bit_identical(cuda):
+    """At most 64 rows the launch spreads each row's heads over several warps;
+    those rows come out bit-identical to the same rows of a larger launch
+    (one warp per row)."""
+    nq, nkv, D = 16, 8, 128
+    g = torch.Generator(device=cuda).manual_seed(5)
+    big = torch.randn(1, 100, nq + nkv, D, device=cuda, generator=g).to(torch.bfloat16)
+    qw = (1 + 0.2 * torch.randn(D, device=cuda, generator=g)).to(torch.bfloat16)
+    kw = (1 + 0.2 * torch.randn(D, device=cuda, generator=g)).to(torch.bfloat16)
+    cos = torch.randn(1, 100, D, device=cuda, generator=g).to(torch.bfloat16)
+    sin = torch.randn(1, 100, D, device=cuda, generator=g).to(torch.bfloat16)
+    small = big[:, :40].contiguous()
+    ops.qk_norm_rope(big[:, :, :nq], big[:, :, nq:], qw, kw, cos, sin, 1e-6)
+    ops.qk_norm_rope(small[:, :, :nq], small[:, :, nq:], qw, kw, cos[:, :40].contiguous(), sin[:, :40].contiguous(),
+                     1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(small, big[:, :40])
 
 
 def test_qk_norm_rope_append(cuda):

@@ -346,7 +346,9 @@ def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_norm_w: torch.Tensor, k_nor
         _require_cuda(nm, t, torch.bfloat16)
         if t.dim() != 4 or t.shape[-1] != 128 or t.stride(-1) != 1 or t.stride(-2) != 128:
             raise ValueError(f"{nm} must be (B, S, heads, 128) with contiguous heads")
-        if t.stride(0) != t.shape[1] * t.stride(1):
+        # rows are addressed as (b * S + s) * row stride: the batch stride
+        # matters only with more than one batch entry
+        if t.shape[0] > 1 and t.stride(0) != t.shape[1] * t.stride(1):
             raise ValueError(f"{nm} rows must be evenly strided across the batch")
     B, S = q.shape[0], q.shape[1]
     if k.shape[:2] != q.shape[:2]:
