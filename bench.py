@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (BASELINE config 3): a random-init Qwen3-1.7B-architecture model in
+Workload: a random-init Qwen3-1.7B-architecture model in
 bf16 (28 layers, hidden 2048, 16/8 heads, head_dim 128, SwiGLU 6144, RoPE
 theta 1e6, vocab 151936), gate at layer 1 (linear 2048 -> 1 + log-sigmoid),
 one 32768-token prompt of uniform random ids per GPU per step, state span
@@ -36,7 +36,7 @@ Reported (one JSON line from rank 0):
   --gate e2e runs the same workload with the finalized gate instead of the
   synthetic linear one (a seeded E2EGate: SwiGLU scoring branch cloned from
   layer 1, per-layer per-head bias, scaled-softmax query scale); the default
-  is BASELINE's linear gate.
+  is the synthetic linear gate.
 """
 import argparse
 import json
@@ -262,7 +262,7 @@ def run_reference(args):
             "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (uniform random ids, random-init weights)",
             "impl": "reference",
-            "config": {"workload": "BASELINE config 3 (Qwen3-1.7B shape gated prefill), bounded CPU sample",
+            "config": {"workload": "Qwen3-1.7B-shape gated prefill, bounded CPU sample",
                        "model": MODEL, "global_batch": 1, "seq_len": CPU_SAMPLE["seq_len"],
                        "K": CPU_SAMPLE["K"], "gate_layer": GATE_LAYER, "parallelism": "host cores"},
             "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -282,7 +282,7 @@ def main():
     ap.add_argument("--no-phase2-graphs", action="store_true",
                     help="launch the Phase-2 layers eagerly instead of replaying a CUDA graph")
     ap.add_argument("--gate", default="linear", choices=("linear", "e2e"),
-                    help="linear: BASELINE's synthetic gate; e2e: a seeded finalized gate (E2EGate)")
+                    help="linear: the synthetic linear gate; e2e: a seeded finalized gate (E2EGate)")
     ap.add_argument("--profile-step", action="store_true",
                     help="after the warm-up, run ONE step between cudaProfilerStart/Stop and exit "
                          "(for ncu --profile-from-start off); prints no bench line")
@@ -323,7 +323,7 @@ def main():
                                             prompt[STATE_END:].tolist()), dtype=torch.long).pin_memory()
 
     def step_e2e():
-        return tm.generate(host_ids, None, max_kept_prefill_tokens=K_KEEP)
+        return tm.generate(host_ids, None, max_new_tokens=1, max_kept_prefill_tokens=K_KEEP)
 
     meter = KernelMeter()
     meter.install()
@@ -399,7 +399,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms_step, "ttft_ms": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (uniform random ids, random-init weights)",
-        "config": {"workload": "BASELINE config 3: Qwen3-1.7B-shape gated prefill, 32768-token prompt, "
+        "config": {"workload": "Qwen3-1.7B-shape gated prefill, 32768-token prompt, "
                                "state [512, 32512), K=2000, gate layer 1",
                    "model": MODEL, "global_batch": world, "seq_len": SEQ_LEN, "K": K_KEEP,
                    "gate_layer": GATE_LAYER, "gate": args.gate,

@@ -112,12 +112,19 @@ def weights_fp32(model) -> (dict, dict):
 
 def gated_prefill(model, w_gate: torch.Tensor, prompt_ids_list: Sequence[Sequence[int]],
                   starts: Sequence[int], ends: Sequence[int], gate_layer: int, K,
-                  weights=None, bias_bf16: bool = False) -> dict:
+                  weights=None, bias_bf16: bool = False, kept_override=None) -> dict:
     """Returns dict(first_tokens (B,), kept_positions list, n_kepts, K_clampeds,
-    logits (B, vocab) fp32, scores list, phase1_hidden (B, S, H)).
+    logits (B, vocab) fp32, scores list, phase1_hidden (B, S, H),
+    selected_positions list).
 
     bias_bf16: round the Phase-2 bias to bfloat16, as the reference does when
-    the model runs in bf16 (gate_bias_batched has the hidden dtype, :1450)."""
+    the model runs in bf16 (gate_bias_batched has the hidden dtype, :1450).
+    kept_override: per request, the kept positions Phase 2 runs on instead of
+    this oracle's own selection (prefix, K_clamped state tokens, suffix, in
+    ascending order; the bias is this oracle's score at those state tokens).
+    The oracle's own selection is returned as selected_positions either way,
+    so one call gives both the selection to compare and Phase-2 logits on
+    another implementation's kept rows."""
     layers, g, cfg = weights if weights is not None else weights_fp32(model)
     B = len(prompt_ids_list)
     lens = [len(x) for x in prompt_ids_list]
@@ -132,13 +139,19 @@ def gated_prefill(model, w_gate: torch.Tensor, prompt_ids_list: Sequence[Sequenc
         h = _layer(h, layers[i], cfg, cos, sin, None)
     w64 = w_gate.detach().double().reshape(-1).cpu()
     Ks = list(K) if isinstance(K, (list, tuple)) else [K] * B
-    kept, scores, n_kepts, K_cl = [], [], [], []
+    kept, scores, n_kepts, K_cl, selected = [], [], [], [], []
     for b in range(B):
         n_art = ends[b] - starts[b]
         sc = torch.nn.functional.logsigmoid(h[b, starts[b]:ends[b]].double() @ w64).float()
         kc = max(1, min(int(Ks[b]), n_art))
         top = torch.as_tensor(topk_indices(sc.numpy(), kc), dtype=torch.long)
         keep = torch.cat([torch.arange(starts[b]), starts[b] + top, torch.arange(ends[b], lens[b])])
+        selected.append(keep.tolist())
+        if kept_override is not None:
+            keep = torch.as_tensor(list(kept_override[b]), dtype=torch.long)
+            if len(keep) != len(selected[-1]):
+                raise ValueError(f"request {b}: kept_override has {len(keep)} positions, "
+                                 f"the selection {len(selected[-1])}")
         kept.append(keep)
         scores.append(sc)
         n_kepts.append(len(keep))
@@ -163,7 +176,7 @@ def gated_prefill(model, w_gate: torch.Tensor, prompt_ids_list: Sequence[Sequenc
     logits = last @ g["lm_head"].T
     return dict(first_tokens=logits.argmax(-1), kept_positions=[k.tolist() for k in kept],
                 n_kepts=n_kepts, K_clampeds=K_cl, logits=logits, scores=scores,
-                phase1_hidden=phase1_hidden, bias=bias)
+                phase1_hidden=phase1_hidden, bias=bias, selected_positions=selected)
 
 
 def gated_prefill_e2e(model, gate: dict, prompt_ids_list: Sequence[Sequence[int]],

@@ -10,7 +10,7 @@
  *                        tokengate/e2e_gate/gate_module/gate_forward.py:1396-1407,
  *                        with the fp32 readout fixture of
  *                        tests/inference/test_prefill_memory.py:18-33 plus
- *                        the log-sigmoid BASELINE's config 2 names);
+ *                        the log-sigmoid of the gate-scoring workload);
  *   oracle_topk_select  torch.topk + keep-list + Phase-2 bias row
  *                       (gate_forward.py:84-99, :1409-1421, :968-1036, :1463-1469),
  *                       ordering (score desc, index asc);

@@ -173,7 +173,7 @@ def test_generate_api_decodes_and_stops_at_eos(tiny, cuda):
     ids = with_state_span(list(range(5)), list(range(100, 400)), list(range(7)))
     out = tm.generate(ids, None, max_kept_prefill_tokens=25, max_new_tokens=6)
     assert len(out.token_ids[0]) == 6 and out.decode_s > 0
-    first = tm.generate(ids, None, max_kept_prefill_tokens=25)
+    first = tm.generate(ids, None, max_kept_prefill_tokens=25, max_new_tokens=1)
     assert out.token_ids[0][0] == first.token_ids[0][0]
 
     class Tok:

@@ -154,3 +154,42 @@ def test_backend_names():
     for bad in ("flex", "sdpa", "cudnn", "aug-fa4"):
         with pytest.raises(ValueError):
             resolve_backend(bad, causal=False)
+
+
+def test_resolve_gate_path_run_directory(tmp_path):
+    """A run directory resolves to its newest-stage gate (tokengate/inference.py:38-59):
+    swa_gate_* > gate_final > gate_step*, the last of each sorted; a .pt path
+    must exist; a spec that is neither (a Hub id) is an error offline."""
+    from tokengate_b200.inference import resolve_gate_path
+    d = tmp_path / "run"
+    d.mkdir()
+    with pytest.raises(FileNotFoundError):
+        resolve_gate_path(str(d))                      # no gate in it yet
+    for n in ("gate_step100.pt", "gate_step200.pt"):
+        (d / n).write_bytes(b"x")
+    assert resolve_gate_path(str(d)) == str(d / "gate_step200.pt")
+    (d / "gate_final.pt").write_bytes(b"x")
+    assert resolve_gate_path(str(d)) == str(d / "gate_final.pt")
+    for n in ("swa_gate_a.pt", "swa_gate_b.pt"):
+        (d / n).write_bytes(b"x")
+    assert resolve_gate_path(d) == str(d / "swa_gate_b.pt")
+    assert resolve_gate_path(str(d / "gate_final.pt")) == str(d / "gate_final.pt")
+    with pytest.raises(FileNotFoundError):
+        resolve_gate_path(str(d / "missing.pt"))
+    with pytest.raises(FileNotFoundError, match="offline"):
+        resolve_gate_path("liana313/tokengate-some-repo")
+
+
+def test_load_model_from_run_directory_cpu(tmp_path):
+    """load_model(run_dir) loads the directory's newest linear gate and its metadata."""
+    from tokengate_b200.inference import load_model
+    small = dict(hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=2,
+                 num_key_value_heads=1, head_dim=128, vocab_size=300, rope_theta=1e6)
+    d = tmp_path / "run"
+    d.mkdir()
+    for name, fill in (("gate_step10.pt", 1.0), ("gate_final.pt", 2.0)):
+        torch.save({"state_dict": {"readout.weight": torch.full((1, 256), fill)},
+                    "metadata": {"gate_layer": 1}}, d / name)
+    tm = load_model(str(d), base_model=small, device="cpu")
+    assert tm.gate_layer == 1
+    assert torch.equal(tm.gate.readout.weight.detach(), torch.full((1, 256), 2.0))

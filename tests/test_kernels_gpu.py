@@ -87,7 +87,7 @@ def test_attention_shapes(cuda, B, S, Hq, Hkv, bias_kind):
 
 
 def test_attention_config1_rows(cuda):
-    """BASELINE config 1 shape: B=1, S=4096, 16/8 heads; bias logsigmoid(2N) on the state span."""
+    """The key-bias op workload: B=1, S=4096, 16/8 heads; bias logsigmoid(2N) on the state span."""
     g = torch.Generator().manual_seed(0)
     S = 4096
     q = torch.randn(1, S, 16, 128, generator=g).to(torch.bfloat16).to(cuda)
@@ -191,7 +191,7 @@ def test_gate_score_bit_exact(cuda, H):
 
 
 def test_gate_score_config2(cuda):
-    """(1, 32768, 2048) bf16 N(0,1), state 512..32511, w ~ N(0, 1/2048)."""
+    """The gate-scoring workload: (1, 32768, 2048) bf16 N(0,1), state 512..32511, w ~ N(0, 1/2048)."""
     g = torch.Generator().manual_seed(2)
     h = torch.randn(1, 32768, 2048, generator=g).to(torch.bfloat16)
     w = torch.randn(2048, generator=g) / 2048 ** 0.5

@@ -176,12 +176,16 @@ def test_generate_api(tiny, cuda):
     model, gate = tiny["model"], tiny["gate"]
     tm = TokenGateModel(model, gate, 1, "tiny")
     ids = with_state_span(list(range(5)), list(range(100, 400)), list(range(7)))
-    out = tm.generate(ids, None, max_kept_prefill_tokens=25)
+    out = tm.generate(ids, None, max_kept_prefill_tokens=25, max_new_tokens=1)
     assert out.n_kept == [5 + 25 + 7] and out.n_state == [300]
     assert out.kept_pos[0][:5] == list(range(5)) and out.kept_pos[0][-7:] == list(range(305, 312))
     assert len(out.token_ids[0]) == 1 and out.prefill_s > 0
-    all_keep = tm.generate(ids, None)   # K = all
+    all_keep = tm.generate(ids, None, max_new_tokens=1)   # K = all
     assert all_keep.n_kept == [312]
+    # the reference's default budget: 20 new tokens, the first one the prefill's
+    dflt = tm.generate(ids, None, max_kept_prefill_tokens=25)
+    assert len(dflt.token_ids[0]) == 20 and dflt.decode_s > 0
+    assert dflt.token_ids[0][0] == out.token_ids[0][0] and dflt.kept_pos == out.kept_pos
     with pytest.raises(ValueError):
         tm.generate(ids, None, max_new_tokens=0)
     with pytest.raises(ValueError):
@@ -199,10 +203,10 @@ def test_generate_tensor_ids_match_list_ids(tiny, cuda):
     ids = with_state_span(torch.randint(0, 1000, (6,), generator=g).tolist(),
                           torch.randint(0, 1000, (290,), generator=g).tolist(),
                           torch.randint(0, 1000, (9,), generator=g).tolist())
-    ref = tm.generate(ids, None, max_kept_prefill_tokens=30)
+    ref = tm.generate(ids, None, max_kept_prefill_tokens=30, max_new_tokens=1)
     pinned = torch.tensor(ids, dtype=torch.long).pin_memory()
     for t in (pinned, torch.tensor(ids, dtype=torch.int32), pinned.to(cuda)):
-        got = tm.generate(t, None, max_kept_prefill_tokens=30)
+        got = tm.generate(t, None, max_kept_prefill_tokens=30, max_new_tokens=1)
         assert got.n_kept == ref.n_kept and got.n_state == ref.n_state
         assert got.kept_pos == ref.kept_pos and got.token_ids == ref.token_ids
     with pytest.raises(ValueError):

@@ -3,10 +3,13 @@ device memory where they call it (a host runtime binding the library over
 FFI that owns the GPU's memory pool, or a path where cudaMalloc is not
 allowed). It uses the library's fixed 8 MiB per-device scratch instead of a
 caller workspace; this checks it through the C ABI against tg_decode_attn
-(same kernel, caller workspace) on two calls in a row — the second reusing
-the scratch the first left behind — with the attention tests' tolerance
-(max-abs <= 1e-2, cosine >= 0.9999), and that an oversized problem is
-refused. Kept in a file of its own, collected last."""
+(same kernel, same key chunks, caller workspace) on two calls in a row — the
+second reusing the scratch the first left behind — bit for bit, and both
+against a float32 restatement of the decode math with the decode tests'
+tolerance (max-abs <= 1e-2, cosine >= 0.9999). Also: a cache of at most one
+key chunk (no partials, the scratch unused), a second device when there is
+one (its own scratch address), and that an oversized problem is refused.
+Kept in a file of its own, collected last."""
 import ctypes
 
 import pytest
@@ -44,16 +47,57 @@ def _noalloc(q, k, v, bias, qs, n_valid, n_prefix, n_keys):
     return out
 
 
-def test_noalloc_decode_matches_workspace_entry(cuda):
-    for B, Hq, Hkv, n_prefix, n_keys, seed in ((2, 16, 8, 2768, 2772, 1), (1, 32, 8, 9000, 9001, 2)):
-        q, k, v, bias, qs, n_valid = _case(cuda, B, Hq, Hkv, n_prefix, n_keys, seed)
+def _fp32_ref(q, k, v, n_valid, n_prefix, n_keys, bias, q_scale):
+    """float32 decode math: q' = bf16(q * bf16(qs)); softmax(scale q'.k + bias, pads -inf) V."""
+    qf = (q.float().cpu() * q_scale.cpu().to(torch.bfloat16).float()[..., None]).to(torch.bfloat16).float()
+    B, Hq, D = qf.shape
+    G = Hq // k.shape[2]
+    kf = k[:, :n_keys].float().cpu().repeat_interleave(G, dim=2)
+    vf = v[:, :n_keys].float().cpu().repeat_interleave(G, dim=2)
+    s = torch.einsum("bhd,bnhd->bhn", qf, kf) * D ** -0.5
+    m = torch.zeros(B, Hq, n_keys)
+    m[:, :, :n_prefix] = bias.cpu()[..., :n_prefix]
+    for b in range(B):
+        m[b, :, int(n_valid[b]):n_prefix] = float("-inf")
+    return torch.einsum("bhn,bnhd->bhd", torch.softmax(s + m, dim=-1), vf)
+
+
+def _check(got, ref32):
+    err = (got.float().cpu() - ref32).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(got.float().cpu().reshape(-1), ref32.reshape(-1), dim=0).item()
+    assert err <= 1e-2 and cos >= 0.9999, (err, cos)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,n_prefix,n_keys", [
+    (2, 16, 8, 2768, 2772),    # 22 key chunks: partials in the scratch
+    (1, 32, 8, 9000, 9001),
+    (3, 16, 8, 100, 120),      # one chunk: no partials, the scratch unused
+])
+def test_noalloc_decode_matches_workspace_entry(cuda, B, Hq, Hkv, n_prefix, n_keys):
+    q, k, v, bias, qs, n_valid = _case(cuda, B, Hq, Hkv, n_prefix, n_keys, n_keys)
+    ref = ops.decode_attention(q, k, v, n_valid, n_prefix, n_keys, bias=bias, q_scale=qs)
+    ref32 = _fp32_ref(q, k, v, n_valid.cpu(), n_prefix, n_keys, bias, qs)
+    for _ in range(2):   # the second call reuses what the first left in the scratch
         got = _noalloc(q, k, v, bias, qs, n_valid, n_prefix, n_keys)
-        ref = ops.decode_attention(q, k, v, n_valid, n_prefix, n_keys, bias=bias, q_scale=qs)
         torch.cuda.synchronize()
         assert ops.device_error() == 0
-        err = (got.float() - ref.float()).abs().max().item()
-        cos = torch.nn.functional.cosine_similarity(got.float().reshape(-1), ref.float().reshape(-1), dim=0)
-        assert err <= 1e-2 and cos.item() >= 0.9999, (B, n_keys, err, cos.item())
+        assert torch.equal(got, ref), "no-alloc and workspace entry points differ"
+        _check(got, ref32)
+
+
+def test_noalloc_decode_second_device():
+    """The scratch address is looked up per device: a call on cuda:1 after calls on cuda:0."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    dev = torch.device("cuda", 1)
+    with torch.cuda.device(dev):
+        q, k, v, bias, qs, n_valid = _case(dev, 2, 16, 8, 2768, 2772, 5)
+        for _ in range(2):
+            got = _noalloc(q, k, v, bias, qs, n_valid, 2768, 2772)
+            ref = ops.decode_attention(q, k, v, n_valid, 2768, 2772, bias=bias, q_scale=qs)
+            torch.cuda.synchronize(dev)
+            assert torch.equal(got, ref)
+        _check(got, _fp32_ref(q, k, v, n_valid.cpu(), 2768, 2772, bias, qs))
 
 
 def test_noalloc_decode_rejects_oversized(cuda):

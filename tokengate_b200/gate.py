@@ -2,7 +2,7 @@
 
 The reference scores the state span with `gate(h_art.to(gate dtype))` and
 selects on `gate.aggregate(scores)` (tokengate/e2e_gate/gate_module/
-gate_forward.py:1396-1412). BASELINE's synthetic gate is a 2048 -> 1 linear
+gate_forward.py:1396-1412). The benchmarked synthetic gate is a 2048 -> 1 linear
 map with log-sigmoid, i.e. the reference's DeterministicGate fixture
 (tests/inference/test_prefill_memory.py:18-33: fp32 readout, n_layers_bias=0,
 selection_mode "topk", identity aggregate) with log-sigmoid applied.

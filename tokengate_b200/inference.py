@@ -1,19 +1,24 @@
 """Public API: load_model(...) -> TokenGateModel; model.generate(ids, tok, max_kept_prefill_tokens=K).
 
-Mirrors the reference API (tokengate/inference.py:63-180) and its state-span
+Mirrors the reference API (tokengate/inference.py:36-180) and its state-span
 helpers (tokengate/e2e_gate/gate_module/gate_forward.py:664-689):
   * ids carry exactly one STATE_START_ID (-1001) ... STATE_END_ID (-1002) pair
     marking the prunable document; split_state_span strips them and returns
     (clean_ids, start, end), raising ValueError on malformed spans;
-  * generate runs the gated prefill on the B200 kernels and returns a
-    GenerateOutput with the same fields.
-
-Scope: the gated prefill (time to first token). Decoding further tokens
-after the prefill is not part of this build, so max_new_tokens must be 1.
-Checkpoint loading covers the linear log-sigmoid gate (a .pt holding
-{"state_dict": {"readout.weight": (1, hidden)}, "metadata": {...}}); released
-checkpoints with a scoring branch and LoRA adapters are not served.
+  * generate runs the gated prefill on the B200 kernels and, for
+    max_new_tokens > 1 (default 20, as the reference), greedy decoding over
+    the gated KV cache (decode.generate_batch), returning a GenerateOutput
+    with the reference's fields;
+  * load_model takes a gate .pt, or a local run directory in which the
+    newest-stage gate wins (swa_gate_*.pt > gate_final.pt > gate_step*.pt,
+    tokengate/inference.py:38-59). Both gate kinds load: the linear
+    log-sigmoid gate ({"state_dict": {"readout.weight"}, "metadata"}) and the
+    finalized E2EGate with its scoring branch (the reference's save_gate
+    format). A Hugging Face Hub id is rejected with an error: this build
+    runs offline. LoRA adapters of the layers at and below the gate are not
+    served (merged base weights only).
 """
+import glob
 import os
 import re
 import time
@@ -126,8 +131,19 @@ class TokenGateModel:
                                         self.gate_layer, K, prune_below_gate=prune_below_gate)
 
     def generate(self, ids: Union[List[int], List[List[int]]], tokenizer=None, *,
-                 max_new_tokens: int = 1, max_kept_prefill_tokens: Optional[int] = None,
+                 max_new_tokens: int = 20, max_kept_prefill_tokens: Optional[int] = None,
                  streamer=None) -> GenerateOutput:
+        """Gated prefill + greedy decode (tokengate/inference.py:90-134).
+
+        ids : one sequence or a batch (lists, int tensors or arrays), each with
+            the state sentinels (ValueError otherwise).
+        max_new_tokens : generation budget, default 20 like the reference
+            (transformers' default generation length). 1 returns the
+            prefill's first token only (time to first token).
+        max_kept_prefill_tokens : K, the state tokens kept into the cache;
+            None keeps all.
+        streamer : optional put(cpu_ids (B, 1)) / end() receiver.
+        """
         if max_new_tokens < 1:
             raise ValueError("max_new_tokens must be positive")
         if torch.is_tensor(ids) or isinstance(ids, np.ndarray):
@@ -173,7 +189,7 @@ class TokenGateModel:
                               prefill_s=prefill_s, decode_s=0.0, token_ids=tokens)
 
 
-# Qwen3 shapes named by BASELINE's configs (random-init, no checkpoints offline)
+# Qwen3 shapes of the benchmarked models (random-init: no checkpoints offline)
 QWEN3_SHAPES = {
     "qwen3-1.7b": dict(hidden_size=2048, intermediate_size=6144, num_hidden_layers=28,
                        num_attention_heads=16, num_key_value_heads=8, head_dim=128,
@@ -204,12 +220,39 @@ def synthetic_qwen3(name_or_dict, seed: int = 0, device="cuda", dtype=torch.bflo
     return model.to(dtype).eval()
 
 
+def resolve_gate_path(checkpoint: str) -> str:
+    """A checkpoint spec -> the gate .pt file (tokengate/inference.py:38-59).
+
+    A path ending in .pt must be a file. A directory resolves to its
+    newest-stage gate: the last (sorted) swa_gate_*.pt, else gate_final.pt,
+    else the last gate_step*.pt. Anything else would be a Hub repo id, which
+    needs a download: this build has no network path, so it raises
+    FileNotFoundError naming the spec.
+    """
+    checkpoint = os.fspath(checkpoint)
+    if checkpoint.endswith(".pt"):
+        if not os.path.isfile(checkpoint):
+            raise FileNotFoundError(f"gate checkpoint not found: {checkpoint}")
+        return checkpoint
+    if not os.path.isdir(checkpoint):
+        raise FileNotFoundError(
+            f"gate checkpoint {checkpoint!r} is neither a .pt file nor a local run directory "
+            "(Hub ids need a download, which this offline build does not do: fetch the "
+            "repository and pass its directory)")
+    for pat in ("swa_gate_*.pt", "gate_final.pt", "gate_step*.pt"):
+        hits = sorted(glob.glob(os.path.join(checkpoint, pat)))
+        if hits:
+            return hits[-1]
+    raise FileNotFoundError(f"no gate checkpoint (gate_*.pt) in {checkpoint}")
+
+
 def load_model(checkpoint: Optional[str] = None, base_model=None, gate_layer: Optional[int] = None,
                gate_attn: str = "b200", dtype=None, *, model: Optional[torch.nn.Module] = None,
                gate=None, device="cuda", seed: int = 0, trusted_checkpoint: bool = False) -> TokenGateModel:
     """Build a TokenGateModel on the B200 kernels (reference: tokengate/inference.py:141-180).
 
-    checkpoint : a gate .pt. A finalized-gate checkpoint (the reference's
+    checkpoint : a gate .pt or a run directory (resolve_gate_path: newest
+        swa_gate_*.pt > gate_final.pt > gate_step*.pt). A finalized-gate checkpoint (the reference's
         save_gate format: state_dict with gate_branch.* weights and the
         finalized flags) is loaded with gate.load_gate; a linear log-sigmoid
         gate checkpoint ({"state_dict": {"readout.weight"}, "metadata"}) is
@@ -232,8 +275,7 @@ def load_model(checkpoint: Optional[str] = None, base_model=None, gate_layer: Op
     meta = {}
     blob = None
     if checkpoint is not None:
-        if not os.path.isfile(checkpoint):
-            raise FileNotFoundError(f"gate checkpoint not found: {checkpoint}")
+        checkpoint = resolve_gate_path(checkpoint)
         blob = torch.load(checkpoint, map_location="cpu", weights_only=not trusted_checkpoint)
         meta = blob.get("metadata", {}) if isinstance(blob, dict) else {}
     if base_model is None:

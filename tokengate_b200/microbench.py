@@ -1,4 +1,4 @@
-"""Single-kernel runs of the four hot-path kernels at BASELINE shapes (timing and ncu captures).
+"""Single-kernel runs of the four hot-path kernels at the benchmarked shapes (timing and ncu captures).
 
     python -m tokengate_b200.microbench attn   [--seq 32768] [--batch 1] [--hq 16] [--hkv 8] [--iters 20]
     python -m tokengate_b200.microbench score  [--seq 32768] [--batch 1] [--iters 20]
@@ -20,7 +20,7 @@ scores and kept positions read once + both fp32 (L', B, H, n_alloc) tables
 written; decode: the K and V rows of the n_keys cached tokens + q, bias
 row and output, timed as 20 launches in one CUDA graph so the host launch
 path is not what is measured). generate: the gated generation of the
-BASELINE config-3 model (Qwen3-1.7B shape, random init) — prefill seconds
+Qwen3-1.7B-shape model (random init) — prefill seconds
 and decode milliseconds per token.
 """
 import argparse

@@ -1,6 +1,6 @@
 """Request-sharded batched serving of gated prefills on the GPUs of one node.
 
-N independent long-context requests, sharded across the
+The serving sweep: N independent long-context requests, sharded across the
 GPUs (one process per GPU, one model replica each; requests are independent,
 so no collective touches the data path), each GPU serving its share in
 static batches. Mirrors:
