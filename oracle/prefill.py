@@ -17,6 +17,7 @@ Restates, independently of tokengate_b200's modules:
 Scores are logsigmoid(w . h) with h the float32 layer-L output, evaluated in
 float64 and rounded to float32; selection by (score desc, index asc).
 """
+import time
 from typing import Dict, List, Sequence
 
 import torch
@@ -55,20 +56,32 @@ def _attention(q, k, v, bias_bs, chunk=256, q_scale=None):
     keys = torch.arange(S)
     for c0 in range(0, S, chunk):
         c1 = min(S, c0 + chunk)
-        s = (qq[:, :, c0:c1] @ kk) * (D ** -0.5)
+        # a query chunk sees the key prefix [0, c1) only (causal)
+        s = (qq[:, :, c0:c1] @ kk[..., :c1]) * (D ** -0.5)
         if bias_bs is not None:
-            s = s + (bias_bs[:, None, None, :] if bias_bs.dim() == 2 else bias_bs[:, :, None, :])
-        s = s.masked_fill(keys[None, None, None, :] > torch.arange(c0, c1)[None, None, :, None],
+            s = s + (bias_bs[:, None, None, :c1] if bias_bs.dim() == 2 else bias_bs[:, :, None, :c1])
+        s = s.masked_fill(keys[None, None, None, :c1] > torch.arange(c0, c1)[None, None, :, None],
                           float("-inf"))
-        out[:, :, c0:c1] = torch.softmax(s, dim=-1) @ vv
+        out[:, :, c0:c1] = torch.softmax(s, dim=-1) @ vv[:, :, :c1]
     return out.permute(0, 2, 1, 3)
 
 
-def _layer(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs, q_scale=None):
-    return _mlp_half(_attn_half(h, p, cfg, cos, sin, bias_bs, q_scale), p, cfg)
+def _attention_sdpa_compat(q, k, v, bias_bs, q_scale=None):
+    """The reference's CPU attention path, sdpa_compat.sdpa_causal (query
+    chunks of 128 rows, F.scaled_dot_product_attention with an additive
+    bias + causal mask), on (B, S, H, D) tensors; scalar-per-key bias (B, S)."""
+    from .cpu_paths import sdpa_causal
+    if q_scale is not None or (bias_bs is not None and bias_bs.dim() != 2):
+        raise ValueError("the sdpa_compat path here takes a (B, S) bias and no query scale")
+    o = sdpa_causal(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), bias_bs, per_head=False)
+    return o.transpose(1, 2)
 
 
-def _attn_half(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs, q_scale=None):
+def _layer(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs, q_scale=None, attn=None):
+    return _mlp_half(_attn_half(h, p, cfg, cos, sin, bias_bs, q_scale, attn), p, cfg)
+
+
+def _attn_half(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs, q_scale=None, attn=None):
     B, S, _ = h.shape
     D = cfg["head_dim"]
     eps = cfg["rms_norm_eps"]
@@ -81,7 +94,7 @@ def _attn_half(h, p: Dict[str, torch.Tensor], cfg, cos, sin, bias_bs, q_scale=No
     c, s_ = cos[:, :, None, :], sin[:, :, None, :]
     q = q * c + _rot_half(q) * s_
     k = k * c + _rot_half(k) * s_
-    a = _attention(q, k, v, bias_bs, q_scale=q_scale).reshape(B, S, -1)
+    a = (attn or _attention)(q, k, v, bias_bs, q_scale=q_scale).reshape(B, S, -1)
     return h + a @ p["self_attn.o_proj.weight"].T
 
 
@@ -251,3 +264,57 @@ def gated_prefill_e2e(model, gate: dict, prompt_ids_list: Sequence[Sequence[int]
     logits = last @ g["lm_head"].T
     return dict(first_tokens=logits.argmax(-1), kept_positions=[k.tolist() for k in kept],
                 n_kepts=n_kepts, K_clampeds=K_cl, logits=logits, raw_scores=raws)
+
+
+def prefill_by_parts(weights, ids: Sequence[int], start: int, end: int, gate_layer: int, K: int,
+                     w_gate: torch.Tensor, bias_bf16: bool = True, attention: str = "sdpa_compat") -> dict:
+    """One request's gated prefill on the CPU, timed by parts, for a CPU
+    baseline at a prompt length the whole run would take minutes at.
+
+    Runs, once each and in order, the parts gated_prefill runs: the token
+    embedding, ONE Phase-1 layer (layer 0) on the full prompt, the scoring /
+    selection / compaction of the state span on that layer's output, ONE
+    Phase-2 layer (layer gate_layer + 1) on the kept rows with the key bias
+    and the kept positions' RoPE, and the head. Every Phase-1 layer has the
+    same shapes and work (as does every Phase-2 layer), so the whole prefill
+    takes embed + (gate_layer + 1) * phase1_layer + select + (n_layers -
+    gate_layer - 1) * phase2_layer + head; that sum is returned as total_s,
+    with each part's seconds. attention: "sdpa_compat" runs the attention
+    the way the reference does on a CPU (its sdpa_compat chunks), "oracle"
+    this module's float32 restatement."""
+    attn = _attention_sdpa_compat if attention == "sdpa_compat" else _attention
+    layers, g, cfg = weights
+    S = len(ids)
+    t = {}
+    t0 = time.perf_counter()
+    h = g["embed"][torch.as_tensor(list(ids), dtype=torch.long)][None]
+    pos = torch.arange(S)[None]
+    cos, sin = _rope_cos_sin(pos, cfg["head_dim"], cfg["rope_theta"])
+    t["embed"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    h = _layer(h, layers[0], cfg, cos, sin, None, attn=attn)
+    t["phase1_layer"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    w64 = w_gate.detach().double().reshape(-1).cpu()
+    sc = torch.nn.functional.logsigmoid(h[0, start:end].double() @ w64).float()
+    kc = max(1, min(int(K), end - start))
+    top = torch.as_tensor(topk_indices(sc.numpy(), kc), dtype=torch.long)
+    keep = torch.cat([torch.arange(start), start + top, torch.arange(end, S)])
+    hp = h[:, keep]
+    bias = torch.zeros(1, len(keep))
+    bias[0, start:start + kc] = sc[top]
+    if bias_bf16:
+        bias = bias.to(torch.bfloat16).float()
+    cos2, sin2 = _rope_cos_sin(keep[None], cfg["head_dim"], cfg["rope_theta"])
+    t["select"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    hp = _layer(hp, layers[gate_layer + 1], cfg, cos2, sin2, bias, attn=attn)
+    t["phase2_layer"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    last = _rms(hp[0, -1], g["norm"], cfg["rms_norm_eps"])
+    (last @ g["lm_head"].T).argmax()
+    t["head"] = time.perf_counter() - t0
+    n1 = gate_layer + 1
+    n2 = cfg["n_layers"] - n1
+    total = t["embed"] + n1 * t["phase1_layer"] + t["select"] + n2 * t["phase2_layer"] + t["head"]
+    return dict(parts_s=t, total_s=total, n_kept=len(keep), phase1_layers=n1, phase2_layers=n2)

@@ -190,11 +190,16 @@ def test_prefill_qwen3_1p7b_8192(cuda, monkeypatch):
     res = opre.gated_prefill(tm.model, w, [ids], [s0], [s1], 1, K, weights=opre.weights_fp32(tm.model),
                              bias_bf16=True, kept_override=[gpu_kept])
     overlap = len(set(res["selected_positions"][0]) & set(gpu_kept)) / n
-    assert overlap >= 0.95, f"kept overlap with the fp32 oracle's selection {overlap}"
+    state_overlap = (overlap * n - (n - K)) / K
     ref_logits = res["logits"][0].numpy().astype(np.float64)
     got = logits[-1][0].cpu().numpy().astype(np.float64)
     err = np.abs(got - ref_logits).max()
     cos = float(got @ ref_logits / (np.linalg.norm(got) * np.linalg.norm(ref_logits)))
-    assert err <= 0.15 and cos >= 0.999, f"logits max-abs {err} cosine {cos}"
-    assert int(first[0, 0]) == int(res["first_tokens"][0]), \
-        f"first token {int(first[0, 0])} vs oracle {int(res['first_tokens'][0])}"
+    top2 = np.sort(ref_logits)[-2:]
+    diag = (f"kept overlap {overlap:.4f} (state tokens {state_overlap:.4f}), logits max-abs {err:.4f} "
+            f"cosine {cos:.6f}, first token {int(first[0, 0])} vs oracle {int(res['first_tokens'][0])} "
+            f"(oracle top-2 margin {top2[1] - top2[0]:.4f})")
+    print(diag)
+    assert overlap >= 0.95, diag
+    assert err <= 0.15 and cos >= 0.999, diag
+    assert int(first[0, 0]) == int(res["first_tokens"][0]), diag

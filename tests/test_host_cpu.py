@@ -193,3 +193,27 @@ def test_load_model_from_run_directory_cpu(tmp_path):
     tm = load_model(str(d), base_model=small, device="cpu")
     assert tm.gate_layer == 1
     assert torch.equal(tm.gate.readout.weight.detach(), torch.full((1, 256), 2.0))
+
+
+def test_rotary_frequencies_stay_fp32():
+    """A model cast to bf16 after construction gets float32 rotary frequencies
+    back (patch_model / synthetic_qwen3): the rotary cos at position 30000
+    then matches the float64 angle to bf16 rounding, as a from_pretrained(bf16)
+    model does; with bf16 frequencies it is off by whole turns."""
+    from tokengate_b200.inference import qwen3_config
+    from tokengate_b200.model import patch_model
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3ForCausalLM
+    small = dict(hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=2,
+                 num_key_value_heads=1, head_dim=128, vocab_size=300, rope_theta=1e6)
+    m = Qwen3ForCausalLM(qwen3_config(small)).to(torch.bfloat16)
+    pos = torch.tensor([[0, 1000, 8000, 30000]])
+    inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float64) / 128))
+    ang = pos[0, :, None].double() * inv
+    x = torch.zeros(1, 4, 256, dtype=torch.bfloat16)
+    c_bad, _ = m.model.rotary_emb(x, pos)
+    assert (c_bad[0, :, :64].double() - ang.cos()).abs().max() > 0.5
+    patch_model(m)
+    assert m.model.rotary_emb.inv_freq.dtype == torch.float32
+    c, s = m.model.rotary_emb(x, pos)
+    assert (c[0, :, :64].double() - ang.cos()).abs().max() < 1.5e-2
+    assert (s[0, :, :64].double() - ang.sin()).abs().max() < 1.5e-2

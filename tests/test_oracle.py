@@ -132,3 +132,44 @@ def test_prefill_oracle_matches_reference():
         assert res["kept_positions"][b] == d["kept"][b, :n].tolist()
     assert res["first_tokens"].tolist() == d["first_tokens"].tolist()
     np.testing.assert_allclose(res["logits"].numpy(), d["logits"], atol=2e-4, rtol=1e-4)
+
+
+def test_cpu_paths_match_reference_fixtures():
+    """The CPU-baseline restatements (oracle/cpu_paths.py) reproduce the
+    reference's own FlexAttention key-bias outputs and sdpa_causal outputs."""
+    import oracle.cpu_paths as ocp
+    d = _load("attn_d128.npz")
+    q, k, v = (torch.from_numpy(_bf16_bits_to_f32(d[n])) for n in ("q_bf16", "k_bf16", "v_bf16"))
+    for key, bias, per_head in (("flex_h", d["bias_h"], True), ("flex_s", d["bias_s"], False)):
+        b = torch.from_numpy(np.ascontiguousarray(bias))
+        out = ocp.flex_keybias_attention(q, k, v, b, per_head=per_head).numpy()
+        np.testing.assert_allclose(out, d[key], atol=2e-5, rtol=1e-5, err_msg=key)
+        out2 = ocp.sdpa_causal(q, k, v, b, per_head=per_head).numpy()
+        np.testing.assert_allclose(out2, d[key], atol=2e-5, rtol=1e-5, err_msg=f"sdpa {key}")
+    s = _load("attn_sdpa_small.npz")
+    for kvh in (1, 2, 4):
+        qq, kk, vv = (torch.from_numpy(s[f"kv{kvh}_{n}"]) for n in "qkv")
+        for tag, per_head in (("s", False), ("bs", False), ("sh", True), ("bsh", True)):
+            b = torch.from_numpy(s[f"kv{kvh}_{tag}_bias"])
+            ref = s[f"kv{kvh}_{tag}_out"]
+            np.testing.assert_allclose(ocp.sdpa_causal(qq, kk, vv, b, per_head=per_head, chunk_size=5).numpy(),
+                                       ref, atol=1e-5, rtol=1e-5, err_msg=f"kv{kvh} {tag}")
+            np.testing.assert_allclose(ocp.flex_keybias_attention(qq, kk, vv, b, per_head=per_head).numpy(),
+                                       ref, atol=1e-5, rtol=1e-5, err_msg=f"flex kv{kvh} {tag}")
+
+
+def test_cpu_gate_select_compact_matches_oracle_selection():
+    """The reference-ops CPU leg keeps what the selection oracle keeps on untied scores."""
+    import oracle.cpu_paths as ocp
+    g = torch.Generator().manual_seed(5)
+    S, H = 600, 256
+    hidden = torch.randn(S, H, generator=g).to(torch.bfloat16)
+    w = torch.randn(H, generator=g) / H ** 0.5
+    kv = [torch.randn(2, S, 128, generator=g).to(torch.bfloat16) for _ in range(2)]
+    r = ocp.gate_select_compact(hidden, w, 40, 560, 77, kv)
+    sc = r["scores"].numpy()
+    assert len(np.unique(sc)) == len(sc)
+    keep, _, _, nk = osel.topk_select(sc, 77, 40, S, 40 + 77 + 40)
+    assert r["keep"].tolist() == keep[:nk].tolist()
+    assert torch.equal(r["hidden"], hidden[r["keep"]])
+    assert torch.equal(r["kv"][1], kv[1][:, r["keep"]])

@@ -145,6 +145,18 @@ def check(status: int) -> None:
     raise TokenGateKernelError(status, msg)
 
 
+# C-ABI calls that launched kernels since import (host-side count; each such
+# call of the prefill path launches one kernel at up to 64 requests)
+LAUNCH_CALLS = 0
+
+
+def check_launch(status: int) -> None:
+    """check() for a call that launches kernels, counted in LAUNCH_CALLS."""
+    global LAUNCH_CALLS
+    LAUNCH_CALLS += 1
+    check(status)
+
+
 def device_error(stream_handle: int = 0, clear: bool = False) -> int:
     """Bit flags recorded on the current device by kernels whose bounded waits gave up."""
     out = ctypes.c_uint(0)

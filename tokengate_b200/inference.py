@@ -29,7 +29,7 @@ import numpy as np
 import torch
 
 from .gate import SYNTHETIC_E2E_SEED, LinLogSigGate, load_gate, synthetic_e2e_gate
-from .model import patch_model, set_attention_backends_for_layers
+from .model import patch_model, rope_inv_freq_fp32, set_attention_backends_for_layers
 from .prefill import prefill_batch_for_decode
 
 STATE_START_ID = -1001
@@ -217,7 +217,9 @@ def synthetic_qwen3(name_or_dict, seed: int = 0, device="cuda", dtype=torch.bflo
     torch.manual_seed(seed)
     with torch.device(device):
         model = Qwen3ForCausalLM(cfg)
-    return model.to(dtype).eval()
+    model = model.to(dtype).eval()
+    rope_inv_freq_fp32(model)     # the cast above also cast the rotary frequencies
+    return model
 
 
 def resolve_gate_path(checkpoint: str) -> str:

@@ -67,6 +67,102 @@ def _graph_time(fn, n, reps, warmup=3):
     return e0.elapsed_time(e1) / (reps * n)
 
 
+class _L2Flush:
+    """A 256 MB buffer (twice the L2) written before each timed launch."""
+
+    def __init__(self, dev):
+        self.buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.buf.zero_()
+
+
+def _time_flushed(fn, flush, iters=10, warmup=3):
+    """Median CUDA-event ms of one fn() launch, L2 flushed before each."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
+def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> dict:
+    """Single-kernel figures of the hot-path kernels at the benchmarked shapes,
+    timed with CUDA events (median of `iters` launches, L2 flushed before each).
+
+    attention: B=1, 16/8 heads, causal, S = 4096 (per-key bias: log-sigmoid of
+    N(0,2) logits on [256, 3840), 0 elsewhere), 2768 (a Phase-2 bias row:
+    0 on a 512 prefix / 256 suffix, bf16 scores between), 8192 and 32768
+    (Phase 1: no bias); TFLOP/s of 4*Hq*D*S(S+1)/2 and the fraction of
+    `tflops_peak`. gate score / top-K / gather at 32768 tokens, state
+    [512, 32512), K=2000, for 1 and 8 requests: GB/s of the algorithmic bytes
+    (score: the bf16 state rows + w + fp32 scores; top-K: scores read +
+    kept positions and bias row written; gather: the hidden rows and the K/V
+    rows of two below-gate layers, read and written) and the fraction of
+    `hbm_peak_gbs`."""
+    g = torch.Generator(device=dev).manual_seed(0)
+    flush = _L2Flush(dev)
+    out = {"timing": f"CUDA events, median of {iters} launches, L2 flushed (256 MB write) before each",
+           "attention": [], "gate_score": [], "topk": [], "gather": []}
+    for S, kind in ((4096, "per-key bias"), (2768, "Phase-2 bias row"), (8192, "no bias"), (32768, "no bias")):
+        q = torch.randn(1, S, 16, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        k = torch.randn(1, S, 8, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        v = torch.randn(1, S, 8, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        bias = None
+        if S == 4096:
+            bias = torch.zeros(1, 1, S, device=dev)
+            bias[..., 256:3840] = torch.nn.functional.logsigmoid(
+                2 * torch.randn(3584, device=dev, generator=g))
+        elif S == 2768:
+            bias = torch.zeros(1, 1, S, device=dev)
+            bias[..., 512:2512] = torch.nn.functional.logsigmoid(
+                2 * torch.randn(2000, device=dev, generator=g)).to(torch.bfloat16).float()
+        o = torch.empty_like(q)
+        ms = _time_flushed(lambda: ops.keybias_attention(q, k, v, bias=bias, out=o), flush, iters)
+        flops = 4.0 * 16 * 128 * S * (S + 1) / 2
+        tf = flops / ms / 1e9
+        out["attention"].append(dict(seq=S, heads="16/8", bias=kind, us=ms * 1e3, tflops=tf,
+                                     frac=tf / tflops_peak))
+        del q, k, v, o
+    S, st0, st1, K, H = 32768, 512, 32512, 2000, 2048
+    n_art, n_kept = st1 - st0, st0 + K + (S - st1)
+    for B in (1, 8):
+        h = torch.randn(B, S, H, device=dev, dtype=torch.bfloat16, generator=g)
+        w = torch.randn(H, device=dev, generator=g) / H ** 0.5
+        sc = ops.gate_score(h, w, [st0] * B, [n_art] * B)
+        ms = _time_flushed(lambda: ops.gate_score(h, w, [st0] * B, [n_art] * B, out=sc), flush, iters)
+        byts = B * (n_art * H * 2 + n_art * 4) + H * 4
+        out["gate_score"].append(dict(requests=B, us=ms * 1e3, gbs=byts / ms / 1e6,
+                                      frac=byts / ms / 1e6 / hbm_peak_gbs))
+        keep = torch.empty(B, n_kept, dtype=torch.int64, device=dev)
+        brow = torch.empty(B, n_kept, dtype=torch.bfloat16, device=dev)
+        ms = _time_flushed(lambda: ops.topk_select(sc, [n_art] * B, [K] * B, [st0] * B, [S] * B, n_kept,
+                                                   keep_out=keep, bias_out=brow), flush, iters)
+        byts = B * (n_art * 4 + n_kept * 10)
+        out["topk"].append(dict(requests=B, k=K, us=ms * 1e3, gbs=byts / ms / 1e6,
+                                frac=byts / ms / 1e6 / hbm_peak_gbs))
+        kv = [torch.randn(B, S, 8, 128, device=dev, dtype=torch.bfloat16, generator=g) for _ in range(4)]
+        dh = torch.empty(B, n_kept, H, device=dev, dtype=torch.bfloat16)
+        dkv = [torch.empty(B, n_kept, 8, 128, device=dev, dtype=torch.bfloat16) for _ in range(4)]
+        specs = [ops.gather_spec_rows(h, dh, 1)] + [ops.gather_spec_rows(a, d, 1) for a, d in zip(kv, dkv)]
+        ms = _time_flushed(lambda: ops.gather_rows(specs, keep, [n_kept] * B, n_kept, dev), flush, iters)
+        byts = B * 2 * n_kept * (H * 2 + 4 * 8 * 128 * 2) + B * n_kept * 8
+        out["gather"].append(dict(requests=B, k=K, us=ms * 1e3, gbs=byts / ms / 1e6,
+                                  frac=byts / ms / 1e6 / hbm_peak_gbs))
+        del h, kv, dh, dkv
+    assert ops.device_error() == 0
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=("attn", "score", "topk", "gather", "branch", "tables", "decode",

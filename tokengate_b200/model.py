@@ -178,9 +178,37 @@ def full_attn_layer_indices(model) -> List[int]:
     return [i for i, layer in enumerate(model.model.layers) if hasattr(layer, "self_attn")]
 
 
+def rope_inv_freq_fp32(model: torch.nn.Module) -> None:
+    """Give every rotary embedding of `model` float32 inverse frequencies.
+
+    transformers builds them in float32 and computes the rotary angles
+    position * inv_freq in float32 (Qwen3RotaryEmbedding.forward). A
+    `model.to(torch.bfloat16)` casts these buffers too; bf16 keeps 8
+    significant bits, so the angle of frequency f at position p moves by up to
+    ~p * f * 2^-9 radians: wrong rotations from a few hundred positions on
+    (whole turns at 32k). A model loaded with from_pretrained(dtype=bf16), as
+    the reference loads it, keeps them in float32; this restores that for
+    models cast after construction, recomputing them from the config."""
+    for mod in model.modules():
+        inv = getattr(mod, "inv_freq", None)
+        if not isinstance(inv, torch.Tensor) or inv.dtype == torch.float32 or not hasattr(mod, "config"):
+            continue
+        rope_type = getattr(mod, "rope_type", "default")
+        if rope_type == "default" and hasattr(mod, "compute_default_rope_parameters"):
+            fresh, _ = mod.compute_default_rope_parameters(mod.config, inv.device)
+        else:
+            from transformers.modeling_rope_utils import ROPE_INIT_FUNCTIONS
+            fresh, _ = ROPE_INIT_FUNCTIONS[rope_type](mod.config, inv.device)
+        mod.inv_freq = fresh.to(torch.float32)
+        if isinstance(getattr(mod, "original_inv_freq", None), torch.Tensor):
+            mod.original_inv_freq = fresh.to(torch.float32).clone()
+
+
 def patch_model(model: torch.nn.Module) -> torch.nn.Module:
     """Route every Qwen3 attention module of `model` through the B200 kernel
-    (the reference's patch_model_with_flex_attention, qwen3_flex_attention.py:924)."""
+    (the reference's patch_model_with_flex_attention, qwen3_flex_attention.py:924);
+    the rotary inverse frequencies are kept in float32 (rope_inv_freq_fp32)."""
+    rope_inv_freq_fp32(model)
     idx = full_attn_layer_indices(model)
     if not idx:
         raise ValueError("patch_model: no full-attention layers found in model")

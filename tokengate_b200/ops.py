@@ -110,7 +110,7 @@ def keybias_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
     L = _lib.lib()
     with _device_ctx(q):
-        _lib.check(L.tg_keybias_attn_fwd(
+        _lib.check_launch(L.tg_keybias_attn_fwd(
             q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
             k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
             v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
@@ -154,7 +154,7 @@ def gate_score(hidden: torch.Tensor, w: torch.Tensor, row_begin: Sequence[int],
             raise ValueError("out must be (B, >= max(row_count)) fp32 with a contiguous last dim")
     L = _lib.lib()
     with _device_ctx(hidden):
-        _lib.check(L.tg_gate_score(hidden.data_ptr(), hidden.stride(0), hidden.stride(1), H,
+        _lib.check_launch(L.tg_gate_score(hidden.data_ptr(), hidden.stride(0), hidden.stride(1), H,
                                    w.data_ptr(), B, _i32_array(row_begin), _i32_array(row_count),
                                    out.data_ptr(), out.stride(0), _stream(hidden)))
     return out
@@ -202,7 +202,7 @@ def topk_select(scores: torch.Tensor, n_state: Sequence[int], k: Sequence[int],
         tl = torch.empty((B, max(int(x) for x in k)), dtype=torch.int64, device=dev)
     L = _lib.lib()
     with _device_ctx(scores):
-        _lib.check(L.tg_topk_select(
+        _lib.check_launch(L.tg_topk_select(
             scores.data_ptr(), scores.stride(0), B, _i32_array(n_state), _i32_array(k),
             _i32_array(state_begin), _i32_array(seq_len), int(n_alloc),
             keep.data_ptr(), keep.stride(0),
@@ -281,7 +281,7 @@ def gather_rows(specs: Sequence[_lib.GatherTensor], idx: torch.Tensor, n_valid: 
     arr = (_lib.GatherTensor * n)(*specs)
     L = _lib.lib()
     with _device_ctx(idx):
-        _lib.check(L.tg_gather_rows(arr, n, idx.data_ptr(), idx.stride(0), B, int(n_rows),
+        _lib.check_launch(L.tg_gather_rows(arr, n, idx.data_ptr(), idx.stride(0), B, int(n_rows),
                                     _i32_array(n_valid), _stream(idx)))
 
 
@@ -328,7 +328,7 @@ def add_rmsnorm(h: torch.Tensor, delta: Optional[torch.Tensor], weight: Optional
         x_ptr, x_ld, w_ptr = x.data_ptr(), H, weight.data_ptr()
     L = _lib.lib()
     with _device_ctx(h):
-        _lib.check(L.tg_add_rmsnorm(hf.data_ptr(), hf.stride(0), d_ptr, d_ld,
+        _lib.check_launch(L.tg_add_rmsnorm(hf.data_ptr(), hf.stride(0), d_ptr, d_ld,
                                     hof.data_ptr() if delta is not None else None,
                                     hof.stride(0) if delta is not None else 0,
                                     x_ptr, x_ld, w_ptr, hf.shape[0], H, float(eps), _stream(h)))
@@ -361,7 +361,7 @@ def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_norm_w: torch.Tensor, k_nor
         raise ValueError("cos and sin must share strides")
     L = _lib.lib()
     with _device_ctx(q):
-        _lib.check(L.tg_qk_norm_rope(q.data_ptr(), q.stride(1), q.shape[2], k.data_ptr(), k.stride(1),
+        _lib.check_launch(L.tg_qk_norm_rope(q.data_ptr(), q.stride(1), q.shape[2], k.data_ptr(), k.stride(1),
                                      k.shape[2], B * S, S, q_norm_w.data_ptr(), k_norm_w.data_ptr(),
                                      cos.data_ptr(), sin.data_ptr(), cos.stride(0), cos.stride(1), 128,
                                      float(eps), _stream(q)))
@@ -397,7 +397,7 @@ def qk_norm_rope_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_nor
             raise ValueError(f"{nm} must be (B, 1, 128) with a contiguous last dim")
     L = _lib.lib()
     with _device_ctx(q):
-        _lib.check(L.tg_qk_norm_rope_append(
+        _lib.check_launch(L.tg_qk_norm_rope_append(
             q.data_ptr(), q.stride(0), q.shape[2], k.data_ptr(), k.stride(0), k.shape[2],
             v.data_ptr(), v.stride(0), B, q_norm_w.data_ptr(), k_norm_w.data_ptr(),
             cos.data_ptr(), sin.data_ptr(), cos.stride(0), cos.stride(1), 128, float(eps),
@@ -413,7 +413,7 @@ def silu_mul(gu: torch.Tensor) -> torch.Tensor:
     out = torch.empty(*lead, inter, dtype=torch.bfloat16, device=gu.device)
     L = _lib.lib()
     with _device_ctx(gu):
-        _lib.check(L.tg_silu_mul(gf.data_ptr(), gf.stride(0), out.data_ptr(), inter, gf.shape[0], inter,
+        _lib.check_launch(L.tg_silu_mul(gf.data_ptr(), gf.stride(0), out.data_ptr(), inter, gf.shape[0], inter,
                                  _stream(gu)))
     return out
 
@@ -459,7 +459,7 @@ def branch_score(gu: torch.Tensor, w_row: torch.Tensor, row_begin: Sequence[int]
             raise ValueError("out must be (B, >= max(row_count)) fp32 with a contiguous last dim")
     L = _lib.lib()
     with _device_ctx(gu):
-        _lib.check(L.tg_branch_score(gu.data_ptr(), gu.stride(0), gu.stride(1), inter, w_row.data_ptr(),
+        _lib.check_launch(L.tg_branch_score(gu.data_ptr(), gu.stride(0), gu.stride(1), inter, w_row.data_ptr(),
                                      B, _i32_array(row_begin), _i32_array(row_count), out.data_ptr(),
                                      out.stride(0), _stream(gu)))
     return out
@@ -501,7 +501,7 @@ def phase2_tables(scores: torch.Tensor, state_begin: Sequence[int], n_state: Seq
     q_scale = torch.empty_like(bias)
     L = _lib.lib()
     with _device_ctx(scores):
-        _lib.check(L.tg_phase2_tables(scores.data_ptr(), scores.stride(0), B, _i32_array(state_begin),
+        _lib.check_launch(L.tg_phase2_tables(scores.data_ptr(), scores.stride(0), B, _i32_array(state_begin),
                                       _i32_array(n_state), keep.data_ptr(), keep.stride(0),
                                       _i32_array(n_kept), int(n_alloc), gs.data_ptr(), at.data_ptr(),
                                       int(Lp), int(H), float(eps), float(gain), bias.data_ptr(),
@@ -574,7 +574,7 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_valid:
         ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device) if nbytes.value else None
         if n_keys_dev is not None:
             _require_cuda("n_keys_dev", n_keys_dev, torch.int32)
-        _lib.check(L.tg_decode_attn_ex(
+        _lib.check_launch(L.tg_decode_attn_ex(
             q.data_ptr(), q.stride(0), q.stride(1), qs_ptr, qsb,
             k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
             v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
@@ -604,6 +604,6 @@ def gemv(x: torch.Tensor, w: torch.Tensor, swiglu: bool = False, out: Optional[t
         out = torch.empty((B, N), dtype=torch.bfloat16, device=x.device)
     L = _lib.lib()
     with _device_ctx(x):
-        _lib.check(L.tg_gemv(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
+        _lib.check_launch(L.tg_gemv(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
                              B, N, K, int(bool(swiglu)), _stream(x)))
     return out

@@ -28,7 +28,7 @@ from typing import Optional
 
 import torch
 
-from . import ops
+from . import _lib, ops
 from .layers import layer_forward, layer_mlp
 from .model import PrefillCache, _CacheLayer
 
@@ -37,6 +37,9 @@ MAX_GRAPHS = 8
 
 _GRAPHS: "OrderedDict[tuple, _Phase2Graph]" = OrderedDict()
 _POOL = None
+# library kernel launches replayed through graphs since import (each replay
+# adds the count its capture recorded)
+REPLAYED_LAUNCHES = 0
 
 
 def _pool():
@@ -71,8 +74,10 @@ class _Phase2Graph:
         torch.cuda.current_stream(device).wait_stream(side)
         self.cache = PrefillCache(n_layers)
         self.graph = torch.cuda.CUDAGraph()
+        n0 = _lib.LAUNCH_CALLS
         with torch.cuda.graph(self.graph, pool=_pool(), stream=side):
             self.out_h, self.out_delta = self._run(self.cache)
+        self.launches = _lib.LAUNCH_CALLS - n0   # library kernels per replay
 
     def _run(self, cache):
         fw, L = self.fw, self.gate_layer
@@ -92,6 +97,8 @@ class _Phase2Graph:
         return h, delta
 
     def replay(self, hs, cos, sin, bias, qs, cache):
+        global REPLAYED_LAUNCHES
+        REPLAYED_LAUNCHES += self.launches
         self.hs.copy_(hs)
         self.cos.copy_(cos)
         self.sin.copy_(sin)
