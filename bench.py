@@ -536,14 +536,18 @@ def main():
                      "traffic_source": ATTN_TRAFFIC_SOURCE},
         "clocks": clk,
     }
+    if world == 1 and rank == 0:
+        from tokengate_b200.microbench import ops_table
+        oclk = ClockSampler(local)
+        oclk.start()
+        line["gpu_ops"] = ops_table(dev, peaks["tflops_burst"], peaks["hbm"])
+        line["gpu_ops"]["clocks"] = oclk.stop()
+        line["gpu_ops"]["peaks"] = (f"{peaks['source']}: bf16 burst {peaks['tflops_burst']} TFLOP/s, "
+                                    f"HBM copy {peaks['hbm']} GB/s (each kernel timed alone)")
     # ---- the serving workload at this N (every rank takes part)
     if not args.no_serving:
         line["serving"] = serving_sweep(tm, dev, world, rank, pg)
     if world == 1 and rank == 0:
-        from tokengate_b200.microbench import ops_table
-        line["gpu_ops"] = ops_table(dev, peaks["tflops_burst"], peaks["hbm"])
-        line["gpu_ops"]["peaks"] = (f"{peaks['source']}: bf16 burst {peaks['tflops_burst']} TFLOP/s, "
-                                    f"HBM copy {peaks['hbm']} GB/s (each kernel timed alone)")
         if not args.no_cpu_baseline:
             del tm
             torch.cuda.empty_cache()

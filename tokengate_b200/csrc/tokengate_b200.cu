@@ -57,6 +57,18 @@ int64_t resident_blocks(int64_t needed, int per_sm) {
   return needed < cap ? (needed < 1 ? 1 : needed) : cap;
 }
 
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device
+// (`flags` is the kernel's own array), so launches inside a stream capture
+// issue no attribute calls.
+template <typename Kern>
+cudaError_t smem_limit_once(Kern kern, int bytes, bool (&flags)[kMaxDevices], int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (flags[dev]) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) flags[dev] = true;
+  return e;
+}
+
 int current_device(int* dev) {
   cudaError_t e = cudaGetDevice(dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -338,30 +350,40 @@ int tg_gate_score(const void* hidden, int64_t h_sb, int64_t h_ss, int hidden_dim
     }
     p.total_rows = p.row_off[nb];
     if (p.total_rows == 0) continue;
-    // resident grid: every warp streams many rows (prefetching the next)
-    int sms = 148;
-    {
-      int dev = 0;
-      if (cudaGetDevice(&dev) == cudaSuccess)
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    }
+    // one CTA per SM, each streaming a contiguous range of rows
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int st;
+    if ((st = device_error_ptr(&p.err))) return st;
     void (*kern)(const tg::ScoreParams) = nullptr;
+    int smem = 0;
+    cudaError_t e = cudaSuccess;
     switch (nv) {
-      case 1: kern = tg::gate_score_kernel<1>; break;
-      case 2: kern = tg::gate_score_kernel<2>; break;
-      case 4: kern = tg::gate_score_kernel<4>; break;
-      case 8: kern = tg::gate_score_kernel<8>; break;
-      case 10: kern = tg::gate_score_kernel<10>; break;
-      case 16: kern = tg::gate_score_kernel<16>; break;
-      default: kern = tg::gate_score_kernel<20>; break;
+#define TG_SCORE_CASE(NV)                                                              \
+      case NV: {                                                                       \
+        static bool attr_set[kMaxDevices] = {};                                        \
+        kern = tg::gate_score_bulk_kernel<NV>;                                         \
+        smem = tg::score_bulk_smem<NV>();                                              \
+        e = smem_limit_once(kern, smem, attr_set, dev);                                \
+        break;                                                                         \
+      }
+      TG_SCORE_CASE(1)
+      TG_SCORE_CASE(2)
+      TG_SCORE_CASE(4)
+      TG_SCORE_CASE(8)
+      TG_SCORE_CASE(10)
+      TG_SCORE_CASE(16)
+      TG_SCORE_CASE(20)
+#undef TG_SCORE_CASE
     }
-    int per_sm = 1;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess || per_sm < 1)
-      per_sm = 1;
-    int64_t blocks = (p.total_rows + 7) / 8;
-    if (blocks > (int64_t)sms * per_sm) blocks = (int64_t)sms * per_sm;
-    kern<<<(unsigned)blocks, 256, 0, s>>>(p);
-    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gate score smem)");
+    int64_t rpc = (p.total_rows + sms - 1) / sms;
+    rpc = (rpc + tg::kScoreRowsPerStage - 1) / tg::kScoreRowsPerStage * tg::kScoreRowsPerStage;
+    p.rows_per_cta = rpc;
+    const int64_t blocks = (p.total_rows + rpc - 1) / rpc;
+    kern<<<(unsigned)blocks, tg::kScoreBulkThreads, smem, s>>>(p);
+    e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gate score launch");
   }
   return TG_OK;
@@ -446,6 +468,7 @@ int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t
     if (m & 15) return fail(TG_ERR_ALIGNMENT, "tensor %d: addresses/strides/seg_bytes not 16-byte multiples", i);
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st;
   for (int b0 = 0; b0 < B; b0 += tg::kGatherMaxReq) {
     const int nb = B - b0 < tg::kGatherMaxReq ? B - b0 : tg::kGatherMaxReq;
     tg::GatherParams p;
@@ -466,16 +489,40 @@ int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t
                     n_valid[b0 + i], n_rows);
       p.n_valid[i] = n_valid[b0 + i];
     }
-    int sms = 148;
-    {
-      int dev = 0;
-      if (cudaGetDevice(&dev) == cudaSuccess)
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t units = (int64_t)nb * n_tensors * n_rows;
+    int64_t row_max = 0;
+    for (int i = 0; i < n_tensors; ++i) {
+      const int64_t rb = tensors[i].seg_bytes * tensors[i].n_seg;
+      row_max = rb > row_max ? rb : row_max;
     }
-    const int64_t warps = (int64_t)nb * n_tensors * n_rows;
-    int64_t blocks = (warps + 7) / 8;
-    if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;  // two resident waves, grid-stride rows
-    tg::gather_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
+    if (row_max <= tg::kGatherStageMax && units < 0x7fffffff) {
+      // bulk-copy kernel: stages sized for the longest row (128-byte multiple)
+      p.stage_bytes = (int)((row_max + 127) / 128 * 128);
+      const int smem = tg::gather_bulk_smem(p.stage_bytes);
+      if ((st = device_error_ptr(&p.err))) return st;
+      static bool attr_set[kMaxDevices] = {};
+      cudaError_t e = smem_limit_once(tg::gather_rows_bulk_kernel, tg::gather_bulk_smem(tg::kGatherStageMax),
+                                      attr_set, dev);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gather smem)");
+      int per_sm = 1;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tg::gather_rows_bulk_kernel, 32, smem) !=
+              cudaSuccess || per_sm < 1)
+        per_sm = 1;
+      const int64_t ctas = (int64_t)sms * per_sm;
+      int64_t upc = (units + ctas - 1) / ctas;
+      if (upc < 8) upc = 8;
+      p.units_per_cta = upc;
+      const int64_t blocks = (units + upc - 1) / upc;
+      tg::gather_rows_bulk_kernel<<<(unsigned)blocks, 32, smem, s>>>(p);
+    } else {
+      const int64_t warps = units;
+      int64_t blocks = (warps + 7) / 8;
+      if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;  // two resident waves, grid-stride rows
+      tg::gather_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gather launch");
   }
