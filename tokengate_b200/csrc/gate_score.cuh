@@ -6,7 +6,7 @@
 // HBM-bound. gate_score_bulk_kernel: one producer warp per CTA streams the
 // CTA's contiguous range of state rows into a ring of shared-memory stages
 // with bulk copies (the TMA engine, one copy per row, completion on an
-// mbarrier per stage), eight consumer warps reduce one row each per stage
+// mbarrier per stage), 16 consumer warps (8 for rows over 4 KB) reduce one row each per stage
 // from shared memory with their slice of w in registers. gate_score_kernel
 // (one warp per row, 16-byte non-allocating loads with a one-row prefetch)
 // is kept for rows that are not 16-byte aligned.
@@ -38,14 +38,19 @@ struct ScoreParams {
   unsigned int* err;
 };
 
-constexpr int kScoreRowsPerStage = 8;  // one row per consumer warp
-constexpr int kScoreBulkThreads = 288;  // 8 consumer warps + 1 producer warp
 constexpr unsigned int ERR_SCORE = 1u << 13;
+// rows per stage (one per consumer warp), stages, threads (consumers + one
+// producer warp) and shared memory of the bulk kernel for NV 16-byte vectors
+// per lane (rows of NV * 512 bytes)
 template <int NV>
-__host__ __device__ constexpr int score_stages() { return NV <= 8 ? 4 : 2; }
+__host__ __device__ constexpr int score_rows() { return NV <= 8 ? 16 : 8; }
+template <int NV>
+__host__ __device__ constexpr int score_stages() { return NV <= 8 ? 3 : 2; }
+template <int NV>
+__host__ __device__ constexpr int score_threads() { return (score_rows<NV>() + 1) * 32; }
 template <int NV>
 __host__ __device__ constexpr int score_bulk_smem() {
-  return score_stages<NV>() * kScoreRowsPerStage * NV * 512 + 16 * score_stages<NV>() + 128;
+  return score_stages<NV>() * score_rows<NV>() * NV * 512 + 16 * score_stages<NV>() + 128;
 }
 
 // exp(-a) for a >= 0 by Cody-Waite reduction a = k ln2 - r, |r| <= ln2/2, and a
@@ -183,7 +188,8 @@ __global__ void __launch_bounds__(256) gate_score_kernel(const ScoreParams p) {
 }
 
 template <int NV>
-__global__ void __launch_bounds__(kScoreBulkThreads, 1) gate_score_bulk_kernel(const ScoreParams p) {
+__global__ void __launch_bounds__(score_threads<NV>(), 1) gate_score_bulk_kernel(const ScoreParams p) {
+  constexpr int kScoreRowsPerStage = score_rows<NV>();
   constexpr int ST = score_stages<NV>();
   constexpr int ROWB = NV * 512;  // bytes of one bf16 row
   extern __shared__ __align__(128) uint8_t s_smem[];

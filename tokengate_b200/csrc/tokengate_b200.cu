@@ -378,11 +378,12 @@ int tg_gate_score(const void* hidden, int64_t h_sb, int64_t h_ss, int hidden_dim
 #undef TG_SCORE_CASE
     }
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gate score smem)");
+    const int rows = nv <= 8 ? 16 : 8, threads = (rows + 1) * 32;  // score_rows / score_threads
     int64_t rpc = (p.total_rows + sms - 1) / sms;
-    rpc = (rpc + tg::kScoreRowsPerStage - 1) / tg::kScoreRowsPerStage * tg::kScoreRowsPerStage;
+    rpc = (rpc + rows - 1) / rows * rows;
     p.rows_per_cta = rpc;
     const int64_t blocks = (p.total_rows + rpc - 1) / rpc;
-    kern<<<(unsigned)blocks, tg::kScoreBulkThreads, smem, s>>>(p);
+    kern<<<(unsigned)blocks, threads, smem, s>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gate score launch");
   }
@@ -468,7 +469,6 @@ int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t
     if (m & 15) return fail(TG_ERR_ALIGNMENT, "tensor %d: addresses/strides/seg_bytes not 16-byte multiples", i);
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int st;
   for (int b0 = 0; b0 < B; b0 += tg::kGatherMaxReq) {
     const int nb = B - b0 < tg::kGatherMaxReq ? B - b0 : tg::kGatherMaxReq;
     tg::GatherParams p;
@@ -489,40 +489,16 @@ int tg_gather_rows(const tg_gather_tensor* tensors, int n_tensors, const int64_t
                     n_valid[b0 + i], n_rows);
       p.n_valid[i] = n_valid[b0 + i];
     }
-    int sms = 148, dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess)
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t units = (int64_t)nb * n_tensors * n_rows;
-    int64_t row_max = 0;
-    for (int i = 0; i < n_tensors; ++i) {
-      const int64_t rb = tensors[i].seg_bytes * tensors[i].n_seg;
-      row_max = rb > row_max ? rb : row_max;
+    int sms = 148;
+    {
+      int dev = 0;
+      if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     }
-    if (row_max <= tg::kGatherStageMax && units < 0x7fffffff) {
-      // bulk-copy kernel: stages sized for the longest row (128-byte multiple)
-      p.stage_bytes = (int)((row_max + 127) / 128 * 128);
-      const int smem = tg::gather_bulk_smem(p.stage_bytes);
-      if ((st = device_error_ptr(&p.err))) return st;
-      static bool attr_set[kMaxDevices] = {};
-      cudaError_t e = smem_limit_once(tg::gather_rows_bulk_kernel, tg::gather_bulk_smem(tg::kGatherStageMax),
-                                      attr_set, dev);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gather smem)");
-      int per_sm = 1;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tg::gather_rows_bulk_kernel, 32, smem) !=
-              cudaSuccess || per_sm < 1)
-        per_sm = 1;
-      const int64_t ctas = (int64_t)sms * per_sm;
-      int64_t upc = (units + ctas - 1) / ctas;
-      if (upc < 8) upc = 8;
-      p.units_per_cta = upc;
-      const int64_t blocks = (units + upc - 1) / upc;
-      tg::gather_rows_bulk_kernel<<<(unsigned)blocks, 32, smem, s>>>(p);
-    } else {
-      const int64_t warps = units;
-      int64_t blocks = (warps + 7) / 8;
-      if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;  // two resident waves, grid-stride rows
-      tg::gather_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
-    }
+    const int64_t warps = (int64_t)nb * n_tensors * n_rows;
+    int64_t blocks = (warps + 7) / 8;
+    if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;  // two resident waves, grid-stride rows
+    tg::gather_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gather launch");
   }
