@@ -13,6 +13,7 @@
     bf16-rounded scores with ties at the K=4000 boundary, and a batch that
     mixes it with a 32000-score request and a tiny one, bit-exact against both
     selection oracles;
+  * attention at the long-context shape: S=131072, 32 query / 8 KV heads;
   * the whole gated prefill of the Qwen3-1.7B-shape model at 8192 tokens,
     state [512, 7936), K=464 (the CPU-sampled workload of bench.py), against
     oracle/prefill.py: gate scores bit-exact against the oracle scorer on
@@ -208,3 +209,20 @@ def test_prefill_qwen3_1p7b_8192(cuda, monkeypatch):
     assert overlap >= 0.95, diag
     assert err <= 0.25 and cos >= 0.999 and top10 >= 8, diag
     assert int(first[0, 0]) == int(res["first_tokens"][0]), diag
+
+
+def test_attention_131k_qwen3_8b_heads(cuda):
+    """The long-context scale-up's dense layers: B=1, S=131072, 32 query / 8 KV
+    heads (GQA group 4), no bias and a per-key bias, against the float64
+    oracle on sampled rows (first, middle and last row blocks, row 131071)."""
+    S = 131072
+    g = torch.Generator().manual_seed(131072)
+    q = torch.randn(1, S, 32, 128, generator=g).to(torch.bfloat16).to(cuda)
+    k = torch.randn(1, S, 8, 128, generator=g).to(torch.bfloat16).to(cuda)
+    v = torch.randn(1, S, 8, 128, generator=g).to(torch.bfloat16).to(cuda)
+    mid = S // 2
+    rows = np.array([0, 1, 127, 128, mid, mid + 1, mid + 127, S - 128, S - 127, S - 2, S - 1])
+    _check_attn(q, k, v, None, causal=True, rows=rows)
+    b = torch.zeros(S)
+    b[512:S - 256] = torch.nn.functional.logsigmoid(2 * torch.randn(S - 768, generator=g))
+    _check_attn(q, k, v, b.view(1, 1, S).to(cuda), causal=True, rows=rows[[0, 4, 10]])

@@ -16,6 +16,7 @@ first tokens on the host).
 """
 import argparse
 import json
+import math
 import os
 import statistics
 import time
@@ -69,7 +70,8 @@ def summarize(records: List[dict], wall_s: float) -> dict:
     ttft = sorted(r["ttft_s"] for r in records)
     tokens = sum(r["n_tokens"] for r in records)
     return dict(requests=len(records), tokens=tokens, wall_s=wall_s, tokens_per_s=tokens / wall_s,
-                p50_ttft_ms=statistics.median(ttft) * 1e3, p90_ttft_ms=ttft[int(0.9 * (len(ttft) - 1))] * 1e3,
+                p50_ttft_ms=statistics.median(ttft) * 1e3,
+                p90_ttft_ms=ttft[min(len(ttft) - 1, max(0, math.ceil(0.9 * len(ttft)) - 1))] * 1e3,
                 max_ttft_ms=ttft[-1] * 1e3)
 
 
