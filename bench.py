@@ -74,12 +74,12 @@ GATE_LAYER = 1
 MODEL = "qwen3-1.7b"
 METRIC = "gated-prefill tokens/s (Qwen3-1.7B shape, 32k ctx, K=2000)"
 # DRAM traffic of one Phase-1 attention launch (B=1, S=32768, Hq=16, Hkv=8),
-# dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture of the
-# same launch shape (1.008 GB read + 0.112 GB written; algorithmic 0.256 +
-# 0.128 GB: K/V re-read by the row blocks that share them)
-ATTN_TRAFFIC_BYTES = 1.120e9
-ATTN_TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:keybias -s 3 -c 1 "
-                       "python -m tokengate_b200.microbench attn --seq 32768 --iters 3")
+# dram__bytes_read.sum + dram__bytes_write.sum of the ncu capture summarised
+# in profiles/keybias_attn_32k.md (0.996 GB read + 0.106 GB written;
+# algorithmic 0.256 + 0.128 GB: K/V re-read by the row blocks that share them)
+ATTN_TRAFFIC_BYTES = 1.102e9
+ATTN_TRAFFIC_SOURCE = ("profiles/keybias_attn_32k.md: ncu --set full --clock-control none -k regex:keybias "
+                       "-s 3 -c 1 python -m tokengate_b200.microbench attn --seq 32768 --iters 3 --no-bias")
 
 
 def _dist():
