@@ -218,6 +218,19 @@ int tg_qk_norm_rope_append(void* q, int64_t ld_q, int n_q_heads, void* k, int64_
 int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_t rows, int64_t inter,
                 void* stream);
 
+/* The Qwen3 MLP up-projection with the SwiGLU fused into its epilogue:
+ *   out[m, c] = bf16(bf16(silu(G[m, c])) * U[m, c]),  G = bf16(x W_gate^T), U = bf16(x W_up^T)
+ * for m < M, c < inter: act_fn(gate_proj(x)) * up_proj(x) of the decoder
+ * layers the reference runs (tokengate/e2e_gate/attn/qwen3_flex_attention.py:
+ * 646-648, modeling_qwen3.Qwen3MLP), replacing the bf16 GEMM into [G | U]
+ * and tg_silu_mul. A persistent tcgen05 GEMM of CTA pairs.
+ * x: bf16 (M, K) row stride ld_x; w_gu: bf16 (2*inter, K) = [W_gate; W_up]
+ * row stride ld_w; out: bf16 (M, inter) row stride ld_out. K a multiple of
+ * 64, inter a multiple of 128; bases 16-byte aligned, strides multiples of 8.
+ * M == 0 returns TG_OK without touching the pointers. */
+int tg_gemm_swiglu(const void* x, int64_t ld_x, const void* w_gu, int64_t ld_w, void* out,
+                   int64_t ld_out, int64_t M, int K, int inter, void* stream);
+
 /*
  * a4 (finalized gate) — readout of the scoring branch:
  *   score[b, r] = bf16( sum_k bf16(bf16(silu(g_k)) * u_k) * w[k] ),  stored as fp32

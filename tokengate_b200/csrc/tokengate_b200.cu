@@ -13,6 +13,7 @@
 #include "../../include/tokengate_b200.h"
 #include "ptx.cuh"
 #include "keybias_attn.cuh"
+#include "gemm_swiglu.cuh"
 #include "gate_score.cuh"
 #include "topk_select.cuh"
 #include "gather_rows.cuh"
@@ -137,6 +138,30 @@ int encode_bshd(CUtensorMap* map, const void* base, int B, int S, int H, int64_t
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TG_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return TG_OK;
+}
+
+// (rows, cols) row-major bf16 matrix with row stride ld (elements) -> 2-D map
+// over (col, row), box (64, box_rows), 128-byte swizzle, zero fill out of
+// bounds.
+int encode_2d_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                   int box_rows, const char* name) {
+  EncodeTiledFn enc = nullptr;
+  int st = get_encode_fn(&enc);
+  if (st) return st;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return fail(TG_ERR_ALIGNMENT, "%s: base address not 16-byte aligned", name);
+  if (ld < cols || (ld & 7) != 0)
+    return fail(TG_ERR_ALIGNMENT, "%s: row stride %lld must be >= %lld and a multiple of 8", name,
+                (long long)ld, (long long)cols);
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TG_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
   return TG_OK;
@@ -667,6 +692,56 @@ int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_
   cudaError_t e = launch_pdl(tg::silu_mul_kernel, dim3((unsigned)blocks), dim3(256), 0,
                              static_cast<cudaStream_t>(stream), p);
   if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
+  return TG_OK;
+}
+
+int tg_gemm_swiglu(const void* x, int64_t ld_x, const void* w_gu, int64_t ld_w, void* out,
+                   int64_t ld_out, int64_t M, int K, int inter, void* stream) {
+  if (M < 0 || K < 1 || inter < 1) return fail(TG_ERR_INVALID_ARGUMENT, "gemm_swiglu: M=%lld K=%d inter=%d",
+                                               (long long)M, K, inter);
+  if (M == 0) return TG_OK;  // empty input: nothing to read or write
+  if (x == nullptr || w_gu == nullptr || out == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "gemm_swiglu: NULL argument");
+  if (K % tg::kGsBK != 0) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: K=%d must be a multiple of 64", K);
+  if (inter % 128 != 0) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: inter=%d must be a multiple of 128", inter);
+  if (M > (int64_t)INT32_MAX - 256) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: M=%lld too large", (long long)M);
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (ld_out & 7) || ld_out < inter)
+    return fail(TG_ERR_ALIGNMENT, "gemm_swiglu: out 16-byte aligned, row stride >= inter and a multiple of 8");
+  CUtensorMap tx, tw;
+  int st;
+  if ((st = encode_2d_bf16(&tx, x, M, K, ld_x, 128, "gemm_swiglu x"))) return st;
+  if ((st = encode_2d_bf16(&tw, w_gu, 2 * (int64_t)inter, K, ld_w, 128, "gemm_swiglu w_gu"))) return st;
+  tg::GemmSwigluParams p;
+  memset(&p, 0, sizeof(p));
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ld_out = ld_out;
+  p.M = (int)M;
+  p.K = K;
+  p.inter = inter;
+  p.n_tiles_n = inter / 128;
+  p.n_tiles_m = (int)((M + 255) / 256);
+  const int64_t n_tiles = (int64_t)p.n_tiles_m * p.n_tiles_n;
+  if (n_tiles > INT32_MAX) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: too many tiles");
+  p.n_tiles = (int)n_tiles;
+  if ((st = device_error_ptr(&p.err))) return st;
+  int dev;
+  if ((st = current_device(&dev))) return st;
+  static bool attr_set[kMaxDevices] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(tg::gemm_swiglu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           tg::kGsSmemBytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_swiglu smem)");
+      attr_set[dev] = true;
+    }
+  }
+  // persistent: one CTA pair per SM pair, or fewer when there are fewer tiles
+  const int64_t clusters = std::max<int64_t>(1, std::min<int64_t>(n_tiles, sm_count() / 2));
+  tg::gemm_swiglu_kernel<<<(unsigned)(2 * clusters), tg::kGsThreads, tg::kGsSmemBytes,
+                           static_cast<cudaStream_t>(stream)>>>(tx, tw, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_swiglu launch");
   return TG_OK;
 }
 

@@ -9,7 +9,7 @@ elementwise kernels per layer around 7 GEMMs. Here one layer is
     qk_norm_rope(q, k)                                      # q/k RMSNorm + RoPE, in place
     a     = keybias_attention(q, k, v, gate bias)           # tcgen05 kernel
     h, x2 = add_rmsnorm(h, a @ Wo^T, post_attention_layernorm)
-    act   = silu_mul(x2 @ [Wgate; Wup]^T)                   # one GEMM + one glue kernel
+    act   = silu(x2 @ Wgate^T) * (x2 @ Wup^T)               # one tcgen05 GEMM, SwiGLU in its epilogue
     delta = act @ Wdown^T                                   # added by the next layer
 
 with the module's own weights: the q/k/v and gate/up weights are
@@ -18,6 +18,10 @@ concatenation, so nothing is duplicated and the model stays usable through
 transformers. Q, K and V are views of the fused [q | k | v] projection; the
 prefill cache keeps the K/V views (and with them the buffer's q part: one
 GEMM instead of two costs that memory, ~11 MB per layer at 2768 tokens).
+The [gate | up] projection runs through tg_gemm_swiglu, whose epilogue
+applies the SwiGLU, so the 2*intermediate-wide projection never reaches HBM
+(shapes it does not serve, K not a multiple of 64 or an intermediate size not
+a multiple of 128, take the cuBLAS GEMM and the silu_mul kernel).
 """
 from typing import Optional
 
@@ -52,6 +56,8 @@ class FusedLayerWeights:
         self.q_norm_w = a.q_norm.weight
         self.k_norm_w = a.k_norm.weight
         self.inter = m.gate_proj.weight.shape[0]
+        # shapes tg_gemm_swiglu serves (K a multiple of 64, inter of 128)
+        self.swiglu_fused = self.inter % 128 == 0 and self.wgu.shape[1] % 64 == 0
 
     @staticmethod
     def _fuse(*lins):
@@ -113,7 +119,11 @@ def layer_attention(lw: FusedLayerWeights, h: torch.Tensor, delta: Optional[torc
 def layer_mlp(lw: FusedLayerWeights, x2: torch.Tensor) -> torch.Tensor:
     """The MLP half on post_attention_layernorm output x2: returns the MLP output
     (not yet added to the residual)."""
-    return F.linear(ops.silu_mul(F.linear(x2, lw.wgu)), lw.wdown)
+    if lw.swiglu_fused:
+        act = ops.gemm_swiglu(x2, lw.wgu, lw.inter)
+    else:
+        act = ops.silu_mul(F.linear(x2, lw.wgu))
+    return F.linear(act, lw.wdown)
 
 
 def layer_forward(lw: FusedLayerWeights, h: torch.Tensor, delta: Optional[torch.Tensor],

@@ -418,6 +418,23 @@ def silu_mul(gu: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def gemm_swiglu(x: torch.Tensor, w_gu: torch.Tensor, inter: int) -> torch.Tensor:
+    """x (..., K), w_gu (2*inter, K) = [W_gate; W_up] -> bf16(bf16(silu(x W_gate^T)) * bf16(x W_up^T)),
+    shape (..., inter): Qwen3MLP's act_fn(gate_proj(x)) * up_proj(x) as one tcgen05 GEMM with the
+    SwiGLU in its epilogue (the [gate | up] projection never reaches HBM)."""
+    _require_cuda("x", x, torch.bfloat16)
+    _require_cuda("w_gu", w_gu, torch.bfloat16)
+    xf, lead = _rows2d("x", x)
+    if w_gu.dim() != 2 or w_gu.stride(1) != 1 or w_gu.shape[0] != 2 * inter or w_gu.shape[1] != xf.shape[1]:
+        raise ValueError(f"w_gu must be (2*inter, K) = ({2 * inter}, {xf.shape[1]}) with a contiguous last dim")
+    out = torch.empty(*lead, inter, dtype=torch.bfloat16, device=x.device)
+    L = _lib.lib()
+    with _device_ctx(x):
+        _lib.check_launch(L.tg_gemm_swiglu(xf.data_ptr(), xf.stride(0), w_gu.data_ptr(), w_gu.stride(0),
+                                           out.data_ptr(), inter, xf.shape[0], xf.shape[1], inter, _stream(x)))
+    return out
+
+
 def device_error(clear: bool = False) -> int:
     """Flags recorded by kernels whose bounded waits gave up on the current device (synchronises)."""
     return _lib.device_error(torch.cuda.current_stream().cuda_stream, clear)
