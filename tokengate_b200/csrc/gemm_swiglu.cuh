@@ -37,8 +37,8 @@ constexpr int kGsThreads = 320;
 constexpr int kGsProducerWarp = 8;
 constexpr int kGsMmaWarp = 9;
 constexpr int kGsStages = 6;
-constexpr int kGsBK = 64;                     // K per stage: one 128-byte swizzle atom of bf16
-constexpr int kGsTileBytes = 128 * kGsBK * 2;  // 16 KB: 128 rows x 64 K of A or of B
+constexpr int kGsBK = 64;                      // K per stage: one 128-byte swizzle atom of bf16
+constexpr int kGsTileBytes = 128 * kGsBK * 2;  // 16 KB: 128 rows x 64 K of A or of B (one TMA box)
 constexpr int kGsStageBytes = 2 * kGsTileBytes;
 
 enum {
@@ -66,25 +66,12 @@ struct GemmSwigluParams {
   unsigned int* err;
 };
 
-#ifndef TG_GS_GROUP_M
-#define TG_GS_GROUP_M 0
-#endif
-// Output tile t -> (row tile, column tile). With a group size G > 0 the
-// tiles walk G row tiles down before moving one column tile right, so the
-// tiles in flight share fewer distinct x rows and weight rows; 0 walks the
-// columns of one row tile first.
+// Output tile t -> (row tile, column tile): the columns of one row tile
+// first, so the tiles in flight share x rows and the whole weight stays
+// L2-resident (grouping G row tiles per column sweep measured no faster).
 __device__ __forceinline__ void gs_tile(const GemmSwigluParams& p, int t, int& mt, int& nt) {
-  constexpr int G = TG_GS_GROUP_M;
-  if constexpr (G > 0) {
-    const int per_group = G * p.n_tiles_n;
-    const int grp = t / per_group, in = t - grp * per_group;
-    const int m_rows = min(G, p.n_tiles_m - grp * G);
-    mt = grp * G + in % m_rows;
-    nt = in / m_rows;
-  } else {
-    mt = t / p.n_tiles_n;
-    nt = t % p.n_tiles_n;
-  }
+  mt = t / p.n_tiles_n;
+  nt = t % p.n_tiles_n;
 }
 
 // out = bf16(bf16(silu(g)) * u) for fp32 accumulators g and u (each first
@@ -196,16 +183,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
           if (!warp_wait(bar(GB_FULL + s), ph, p.err, ERR_GEMM)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = sbase + s * kGsStageBytes, sb = sa + kGsTileBytes;
+          // one elected lane issues the stage's 4 MMAs and 2 commits as one
+          // straight-line block: electing per MMA made the issue, not the
+          // tensor core, the limit (1394 vs 1591 TFLOP/s at 32768 rows)
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < kGsBK / 16; ++kk) {
-            if (elect_one())
+            for (int kk = 0; kk < kGsBK / 16; ++kk)
               umma_ss_pair(acc, umma_desc_sw128(sa + kk * 32, 16, 1024), umma_desc_sw128(sb + kk * 32, 16, 1024),
                            kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
-          }
-          if (elect_one()) {
             umma_commit_pair(lbar(GB_EMPTY + s));
             umma_commit_pair(fbar(GB_EMPTY + s));
           }
+          __syncwarp();
           if (++s == kGsStages) { s = 0; ph ^= 1u; }
         }
         if (!ok) break;
@@ -243,12 +232,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
         uint32_t* wp = reinterpret_cast<uint32_t*>(w);
 #pragma unroll
         for (int e = 0; e < 16; ++e)
-#ifdef TG_GS_NO_EPI_MATH
-          wp[e] = g[2 * e] ^ u[2 * e + 1];
-#else
           wp[e] = pack_bf16x2(swiglu_bf16(__uint_as_float(g[2 * e]), __uint_as_float(u[2 * e])),
                               swiglu_bf16(__uint_as_float(g[2 * e + 1]), __uint_as_float(u[2 * e + 1])));
-#endif
         if (row < p.M) {
           uint4* dst = reinterpret_cast<uint4*>(p.out + row * p.ld_out + col0 + c * 32);
 #pragma unroll

@@ -702,7 +702,7 @@ int tg_gemm_swiglu(const void* x, int64_t ld_x, const void* w_gu, int64_t ld_w, 
   if (M == 0) return TG_OK;  // empty input: nothing to read or write
   if (x == nullptr || w_gu == nullptr || out == nullptr)
     return fail(TG_ERR_INVALID_ARGUMENT, "gemm_swiglu: NULL argument");
-  if (K % tg::kGsBK != 0) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: K=%d must be a multiple of 64", K);
+  if (K % tg::kGsBK != 0) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: K=%d must be a multiple of %d", K, tg::kGsBK);
   if (inter % 128 != 0) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: inter=%d must be a multiple of 128", inter);
   if (M > (int64_t)INT32_MAX - 256) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: M=%lld too large", (long long)M);
   if ((reinterpret_cast<uintptr_t>(out) & 15) || (ld_out & 7) || ld_out < inter)
