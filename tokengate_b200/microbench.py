@@ -116,11 +116,15 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
     (score: the bf16 state rows + w + fp32 scores; top-K: scores read +
     kept positions and bias row written; gather: the hidden rows and the K/V
     rows of two below-gate layers, read and written) and the fraction of
-    `hbm_peak_gbs`."""
+    `hbm_peak_gbs`. gemm_swiglu: the MLP up-projection with the SwiGLU
+    epilogue at hidden 2048, intermediate 6144 and M = 2768 (Phase 2) and
+    32768 (Phase 1) rows: TFLOP/s of 2*M*2048*12288, beside cuBLAS's bf16
+    GEMM into [gate | up] alone and with the silu_mul kernel after it (the
+    chain it replaces)."""
     g = torch.Generator(device=dev).manual_seed(0)
     flush = _L2Flush(dev)
     out = {"timing": f"CUDA events, median of {iters} launches, L2 flushed (a 256 MB read) before each",
-           "attention": [], "gate_score": [], "topk": [], "gather": []}
+           "attention": [], "gate_score": [], "topk": [], "gather": [], "gemm_swiglu": []}
     for S, kind in ((4096, "per-key bias"), (2768, "Phase-2 bias row"), (8192, "no bias"), (32768, "no bias")):
         q = torch.randn(1, S, 16, 128, device=dev, dtype=torch.bfloat16, generator=g)
         k = torch.randn(1, S, 8, 128, device=dev, dtype=torch.bfloat16, generator=g)
@@ -167,6 +171,20 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
         out["gather"].append(dict(requests=B, k=K, us=ms * 1e3, gbs=byts / ms / 1e6,
                                   frac=byts / ms / 1e6 / hbm_peak_gbs))
         del h, kv, dh, dkv
+    K, inter = 2048, 6144
+    w = (torch.randn(2 * inter, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+    for M in (2768, 32768):
+        x = (torch.randn(M, K, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        flops = 2.0 * M * K * 2 * inter
+        ms = _time_flushed(lambda: ops.gemm_swiglu(x, w, inter), flush, iters)
+        ms_lin = _time_flushed(lambda: torch.nn.functional.linear(x, w), flush, iters)
+        gu = torch.nn.functional.linear(x, w)
+        ms_silu = _time_flushed(lambda: ops.silu_mul(gu), flush, iters)
+        tf, tf_lin = flops / ms / 1e9, flops / ms_lin / 1e9
+        out["gemm_swiglu"].append(dict(rows=M, K=K, inter=inter, us=ms * 1e3, tflops=tf, frac=tf / tflops_peak,
+                                       cublas_gemm_us=ms_lin * 1e3, cublas_gemm_tflops=tf_lin,
+                                       vs_cublas_gemm=tf / tf_lin, cublas_plus_silu_mul_us=(ms_lin + ms_silu) * 1e3))
+        del x, gu
     assert ops.device_error() == 0
     return out
 
@@ -174,7 +192,7 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=("attn", "score", "topk", "gather", "branch", "tables", "decode",
-                                       "generate", "gemv", "gemvchain"))
+                                       "generate", "gemv", "gemvchain", "gemm"))
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--new", type=int, default=64)
     ap.add_argument("--gate", default="linear", choices=("linear", "e2e"))
@@ -208,6 +226,17 @@ def main(argv=None):
         byts = B * ((S + 1) * a.hkv * 128 * 2 * 2 + a.hq * 128 * 4 + (0 if a.no_bias else a.hq * S * 4))
         res.update(seq=S, hq=a.hq, hkv=a.hkv, bias=not a.no_bias, ms=ms, us=ms * 1e3, mbytes=byts / 1e6,
                    gbs=byts / ms / 1e6)
+    elif a.kernel == "gemm":
+        # the MLP up-projection with the SwiGLU epilogue: --seq rows, --hidden K,
+        # --inter intermediate columns; cuBLAS's GEMM into [gate | up] beside it
+        M, K, I = S, a.hidden, a.inter
+        x = (torch.randn(M, K, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        w = (torch.randn(2 * I, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+        ms = _graph_time(lambda: ops.gemm_swiglu(x, w, I), 3, a.iters)
+        ms_ref = _graph_time(lambda: torch.nn.functional.linear(x, w), 3, a.iters)
+        flops = 2.0 * M * K * 2 * I
+        res.update(rows=M, k=K, inter=I, ms=ms, us=ms * 1e3, tflops=flops / ms / 1e9,
+                   cublas_us=ms_ref * 1e3, cublas_tflops=flops / ms_ref / 1e9)
     elif a.kernel == "gemv":
         x = torch.randn(B, a.hidden, device=dev, dtype=torch.bfloat16, generator=g)
         w = (torch.randn(a.n, a.hidden, device=dev, generator=g) / a.hidden ** 0.5).to(torch.bfloat16)
