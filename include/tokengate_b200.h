@@ -231,6 +231,27 @@ int tg_silu_mul(const void* gu, int64_t ld_gu, void* out, int64_t ld_out, int64_
 int tg_gemm_swiglu(const void* x, int64_t ld_x, const void* w_gu, int64_t ld_w, void* out,
                    int64_t ld_out, int64_t M, int K, int inter, void* stream);
 
+/* The decoder layer's attention input projection with the q/k RMSNorm and
+ * RoPE fused into its epilogue:
+ *   out[m, :] = [q heads | k heads | v heads] of bf16(x W_qkv^T), every q and
+ *   k head y <- bf16(w * bf16(y * rsqrt(mean(y^2) + eps))), then rotated:
+ *   y <- bf16(bf16(y * cos) + bf16(rotate_half(y) * sin)) at row m's cos/sin;
+ *   v heads as projected.
+ * = q_norm(q_proj(x)), k_norm(k_proj(x)), apply_rotary_pos_emb and v_proj(x)
+ * of the decoder layers the reference runs (tokengate/e2e_gate/attn/
+ * qwen3_flex_attention.py:539-551), replacing a bf16 GEMM into [q | k | v]
+ * and tg_qk_norm_rope. A persistent tcgen05 GEMM of CTA pairs.
+ * x: bf16 (M, K) row stride ld_x; w_qkv: bf16 ((n_q + 2*n_k)*128, K) =
+ * [W_q; W_k; W_v] row stride ld_w; out: bf16 (M, (n_q + 2*n_k)*128) row
+ * stride ld_out; q_norm_w / k_norm_w: bf16 (128,); cos / sin: bf16, the 128
+ * values of row m = b*seq + s at b*cs_sb + s*cs_ss (M a multiple of seq).
+ * K a multiple of 64; pointers 16-byte aligned, strides multiples of 8.
+ * M == 0 returns TG_OK without touching the pointers. */
+int tg_gemm_qkv_rope(const void* x, int64_t ld_x, const void* w_qkv, int64_t ld_w, void* out, int64_t ld_out,
+                     int64_t M, int K, int n_q_heads, int n_k_heads, const void* q_norm_w, const void* k_norm_w,
+                     const void* cos, const void* sin, int64_t cs_sb, int64_t cs_ss, int seq, float eps,
+                     void* stream);
+
 /*
  * a4 (finalized gate) — readout of the scoring branch:
  *   score[b, r] = bf16( sum_k bf16(bf16(silu(g_k)) * u_k) * w[k] ),  stored as fp32

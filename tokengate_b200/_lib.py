@@ -86,6 +86,8 @@ _SIGNATURES = {
                                _F, _P, _P, _I64, _I64, _P, _P],
     "tg_silu_mul": [_P, _I64, _P, _I64, _I64, _I64, _P],
     "tg_gemm_swiglu": [_P, _I64, _P, _I64, _P, _I64, _I64, _I32, _I32, _P],
+    "tg_gemm_qkv_rope": [_P, _I64, _P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _I64,
+                         _I32, _F, _P],
     "tg_branch_score": [_P, _I64, _I64, _I32, _P, _I32, _P, _P, _P, _I64, _P],
     "tg_phase2_tables": [_P, _I64, _I32, _P, _P, _P, _I64, _P, _I32, _P, _P, _I32, _I32, _F, _F, _P, _P,
                          _P],

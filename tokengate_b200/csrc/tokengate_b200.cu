@@ -13,7 +13,7 @@
 #include "../../include/tokengate_b200.h"
 #include "ptx.cuh"
 #include "keybias_attn.cuh"
-#include "gemm_swiglu.cuh"
+#include "gemm_pair.cuh"
 #include "gate_score.cuh"
 #include "topk_select.cuh"
 #include "gather_rows.cuh"
@@ -224,6 +224,37 @@ cudaError_t launch_gemv(const tg::GemvParams& p, cudaStream_t s, int dev) {
       return launch_gemv_nb<BT, SW, tg::kGemvLongBatch>(p, s, dev);
   }
   return launch_gemv_nb<BT, SW, tg::kGemvBatch>(p, s, dev);
+}
+}  // namespace
+
+namespace {
+// One launch of the CTA-pair GEMM (gemm_pair.cuh): x (M, K) row stride ld_x
+// against the weight rows (w_rows, K) row stride ld_w, the params' epilogue
+// fields already set. Persistent: one CTA pair per SM pair, or fewer when
+// there are fewer tiles.
+template <int kEpi>
+int launch_gemm_pair(const void* x, int64_t ld_x, const void* w, int64_t w_rows, int64_t ld_w,
+                     tg::GemmPairParams& p, void* stream, const char* name) {
+  CUtensorMap tx, tw;
+  int st;
+  if ((st = encode_2d_bf16(&tx, x, p.M, p.K, ld_x, 128, name))) return st;
+  if ((st = encode_2d_bf16(&tw, w, w_rows, p.K, ld_w, 128, name))) return st;
+  p.n_tiles_m = (p.M + 255) / 256;
+  const int64_t n_tiles = (int64_t)p.n_tiles_m * p.n_tiles_n;
+  if (n_tiles > INT32_MAX) return fail(TG_ERR_UNSUPPORTED, "%s: too many tiles", name);
+  p.n_tiles = (int)n_tiles;
+  if ((st = device_error_ptr(&p.err))) return st;
+  int dev;
+  if ((st = current_device(&dev))) return st;
+  static bool attr_set[kMaxDevices] = {};
+  cudaError_t e = smem_limit_once(tg::gemm_pair_kernel<kEpi>, tg::GemmLayout<kEpi>::kSmemBytes, attr_set, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_pair smem)");
+  const int64_t clusters = std::max<int64_t>(1, std::min<int64_t>(n_tiles, sm_count() / 2));
+  tg::gemm_pair_kernel<kEpi><<<(unsigned)(2 * clusters), tg::kGsThreads, tg::GemmLayout<kEpi>::kSmemBytes,
+                              static_cast<cudaStream_t>(stream)>>>(tx, tw, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  return TG_OK;
 }
 }  // namespace
 
@@ -707,42 +738,61 @@ int tg_gemm_swiglu(const void* x, int64_t ld_x, const void* w_gu, int64_t ld_w, 
   if (M > (int64_t)INT32_MAX - 256) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: M=%lld too large", (long long)M);
   if ((reinterpret_cast<uintptr_t>(out) & 15) || (ld_out & 7) || ld_out < inter)
     return fail(TG_ERR_ALIGNMENT, "gemm_swiglu: out 16-byte aligned, row stride >= inter and a multiple of 8");
-  CUtensorMap tx, tw;
-  int st;
-  if ((st = encode_2d_bf16(&tx, x, M, K, ld_x, 128, "gemm_swiglu x"))) return st;
-  if ((st = encode_2d_bf16(&tw, w_gu, 2 * (int64_t)inter, K, ld_w, 128, "gemm_swiglu w_gu"))) return st;
-  tg::GemmSwigluParams p;
+  tg::GemmPairParams p;
   memset(&p, 0, sizeof(p));
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ld_out = ld_out;
   p.M = (int)M;
   p.K = K;
-  p.inter = inter;
   p.n_tiles_n = inter / 128;
-  p.n_tiles_m = (int)((M + 255) / 256);
-  const int64_t n_tiles = (int64_t)p.n_tiles_m * p.n_tiles_n;
-  if (n_tiles > INT32_MAX) return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu: too many tiles");
-  p.n_tiles = (int)n_tiles;
-  if ((st = device_error_ptr(&p.err))) return st;
-  int dev;
-  if ((st = current_device(&dev))) return st;
-  static bool attr_set[kMaxDevices] = {};
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(tg::gemm_swiglu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           tg::kGsSmemBytes);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_swiglu smem)");
-      attr_set[dev] = true;
-    }
-  }
-  // persistent: one CTA pair per SM pair, or fewer when there are fewer tiles
-  const int64_t clusters = std::max<int64_t>(1, std::min<int64_t>(n_tiles, sm_count() / 2));
-  tg::gemm_swiglu_kernel<<<(unsigned)(2 * clusters), tg::kGsThreads, tg::kGsSmemBytes,
-                           static_cast<cudaStream_t>(stream)>>>(tx, tw, p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "gemm_swiglu launch");
-  return TG_OK;
+  p.b_step = 128;     // rank 0: W_gate rows 128*nt..; rank 1: the W_up rows inter + 128*nt..
+  p.b_rank1 = inter;
+  return launch_gemm_pair<tg::EPI_SWIGLU>(x, ld_x, w_gu, 2 * (int64_t)inter, ld_w, p, stream, "gemm_swiglu");
+}
+
+int tg_gemm_qkv_rope(const void* x, int64_t ld_x, const void* w_qkv, int64_t ld_w, void* out, int64_t ld_out,
+                     int64_t M, int K, int n_q_heads, int n_k_heads, const void* q_norm_w, const void* k_norm_w,
+                     const void* cos, const void* sin, int64_t cs_sb, int64_t cs_ss, int seq, float eps,
+                     void* stream) {
+  if (M < 0 || K < 1 || n_q_heads < 1 || n_k_heads < 1 || seq < 1)
+    return fail(TG_ERR_INVALID_ARGUMENT, "gemm_qkv_rope: M=%lld K=%d heads %d/%d seq=%d", (long long)M, K,
+                n_q_heads, n_k_heads, seq);
+  if (M == 0) return TG_OK;
+  if (x == nullptr || w_qkv == nullptr || out == nullptr || q_norm_w == nullptr || k_norm_w == nullptr ||
+      cos == nullptr || sin == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "gemm_qkv_rope: NULL argument");
+  if (K % tg::kGsBK != 0) return fail(TG_ERR_UNSUPPORTED, "gemm_qkv_rope: K=%d must be a multiple of %d", K, tg::kGsBK);
+  if (M % seq != 0) return fail(TG_ERR_INVALID_ARGUMENT, "gemm_qkv_rope: M=%lld rows not whole sequences of %d",
+                                (long long)M, seq);
+  if (M > (int64_t)INT32_MAX - 256) return fail(TG_ERR_UNSUPPORTED, "gemm_qkv_rope: M=%lld too large", (long long)M);
+  const int n_heads = n_q_heads + 2 * n_k_heads;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (ld_out & 7) || ld_out < (int64_t)n_heads * 128)
+    return fail(TG_ERR_ALIGNMENT, "gemm_qkv_rope: out 16-byte aligned, row stride >= heads*128, a multiple of 8");
+  if (((reinterpret_cast<uintptr_t>(q_norm_w) | reinterpret_cast<uintptr_t>(k_norm_w) |
+        reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin)) & 15) || ((cs_sb | cs_ss) & 7))
+    return fail(TG_ERR_ALIGNMENT, "gemm_qkv_rope: gains and cos/sin 16-byte aligned, cos/sin strides multiples of 8");
+  tg::GemmPairParams p;
+  memset(&p, 0, sizeof(p));
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ld_out = ld_out;
+  p.M = (int)M;
+  p.K = K;
+  p.n_tiles_n = (n_heads + 1) / 2;   // two heads per column tile
+  p.b_step = 256;                     // rank 0: head 2*nt, rank 1: head 2*nt + 1
+  p.b_rank1 = 128;
+  p.n_q = n_q_heads;
+  p.n_k = n_k_heads;
+  p.n_heads = n_heads;
+  p.q_w = static_cast<const __nv_bfloat16*>(q_norm_w);
+  p.k_w = static_cast<const __nv_bfloat16*>(k_norm_w);
+  p.cos = static_cast<const __nv_bfloat16*>(cos);
+  p.sin = static_cast<const __nv_bfloat16*>(sin);
+  p.cs_sb = cs_sb;
+  p.cs_ss = cs_ss;
+  p.seq = seq;
+  p.eps = eps;
+  return launch_gemm_pair<tg::EPI_QKV_ROPE>(x, ld_x, w_qkv, (int64_t)n_heads * 128, ld_w, p, stream,
+                                            "gemm_qkv_rope");
 }
 
 int tg_branch_score(const void* gu, int64_t gu_sb, int64_t gu_ss, int inter, const void* w_row,

@@ -5,8 +5,7 @@ patched, tokengate/e2e_gate/attn/qwen3_flex_attention.py:475-652) issues ~30
 elementwise kernels per layer around 7 GEMMs. Here one layer is
 
     h, x  = add_rmsnorm(h, delta_prev, input_layernorm)     # residual add + RMSNorm
-    qkv   = x @ [Wq; Wk; Wv]^T                              # one GEMM
-    qk_norm_rope(q, k)                                      # q/k RMSNorm + RoPE, in place
+    qkv   = rope(qk_norm(x @ [Wq; Wk; Wv]^T))               # one tcgen05 GEMM, q/k RMSNorm + RoPE in its epilogue
     a     = keybias_attention(q, k, v, gate bias)           # tcgen05 kernel
     h, x2 = add_rmsnorm(h, a @ Wo^T, post_attention_layernorm)
     act   = silu(x2 @ Wgate^T) * (x2 @ Wup^T)               # one tcgen05 GEMM, SwiGLU in its epilogue
@@ -18,10 +17,12 @@ concatenation, so nothing is duplicated and the model stays usable through
 transformers. Q, K and V are views of the fused [q | k | v] projection; the
 prefill cache keeps the K/V views (and with them the buffer's q part: one
 GEMM instead of two costs that memory, ~11 MB per layer at 2768 tokens).
-The [gate | up] projection runs through tg_gemm_swiglu, whose epilogue
-applies the SwiGLU, so the 2*intermediate-wide projection never reaches HBM
-(shapes it does not serve, K not a multiple of 64 or an intermediate size not
-a multiple of 128, take the cuBLAS GEMM and the silu_mul kernel).
+The [q | k | v] projection runs through tg_gemm_qkv_rope (the q/k RMSNorm
+and RoPE in its epilogue) and the [gate | up] projection through
+tg_gemm_swiglu (the SwiGLU in its epilogue), so neither the unnormalised
+q/k nor the 2*intermediate-wide projection reaches HBM. Shapes they do not
+serve (hidden not a multiple of 64, an intermediate size not a multiple of
+128) take cuBLAS and the qk_norm_rope / silu_mul kernels.
 """
 from typing import Optional
 
@@ -56,8 +57,9 @@ class FusedLayerWeights:
         self.q_norm_w = a.q_norm.weight
         self.k_norm_w = a.k_norm.weight
         self.inter = m.gate_proj.weight.shape[0]
-        # shapes tg_gemm_swiglu serves (K a multiple of 64, inter of 128)
+        # shapes the fused projection kernels serve (K a multiple of 64, inter of 128)
         self.swiglu_fused = self.inter % 128 == 0 and self.wgu.shape[1] % 64 == 0
+        self.qkv_fused = self.wqkv.shape[1] % 64 == 0
 
     @staticmethod
     def _fuse(*lins):
@@ -104,11 +106,15 @@ def layer_attention(lw: FusedLayerWeights, h: torch.Tensor, delta: Optional[torc
     layer, gate_forward.py:398-418) and x2 = post_attention_layernorm(a)."""
     B, S, H = h.shape
     h, x = ops.add_rmsnorm(h, delta, lw.in_w, lw.eps, h_out=h if delta is not None else None)
-    qkv = F.linear(x, lw.wqkv).view(B, S, lw.n_q + 2 * lw.n_kv, lw.head_dim)
+    if lw.qkv_fused:
+        qkv = ops.gemm_qkv_rope(x, lw.wqkv, lw.n_q, lw.n_kv, lw.q_norm_w, lw.k_norm_w, cos, sin, lw.qk_eps)
+    else:
+        qkv = F.linear(x, lw.wqkv).view(B, S, lw.n_q + 2 * lw.n_kv, lw.head_dim)
     q = qkv[:, :, :lw.n_q]
     k = qkv[:, :, lw.n_q:lw.n_q + lw.n_kv]
     v = qkv[:, :, lw.n_q + lw.n_kv:]
-    ops.qk_norm_rope(q, k, lw.q_norm_w, lw.k_norm_w, cos, sin, lw.qk_eps)
+    if not lw.qkv_fused:
+        ops.qk_norm_rope(q, k, lw.q_norm_w, lw.k_norm_w, cos, sin, lw.qk_eps)
     if cache is not None:
         k, v = cache.update_tok(k, v, layer_idx)
     a = ops.keybias_attention(q, k, v, bias=gate_bias, causal=True, q_row_scale=q_row_scale)

@@ -435,6 +435,43 @@ def gemm_swiglu(x: torch.Tensor, w_gu: torch.Tensor, inter: int) -> torch.Tensor
     return out
 
 
+def gemm_qkv_rope(x: torch.Tensor, w_qkv: torch.Tensor, n_q: int, n_k: int, q_norm_w: torch.Tensor,
+                  k_norm_w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, eps: float) -> torch.Tensor:
+    """x (B, S, K), w_qkv ((n_q + 2*n_k)*128, K) = [W_q; W_k; W_v] -> (B, S, n_q + 2*n_k, 128): the
+    projection with every q and k head RMS-normalised (q_norm_w / k_norm_w) and rotated by cos / sin
+    (B, S, 128) bf16, the v heads as projected: q_norm(q_proj(x)), k_norm(k_proj(x)) with RoPE and
+    v_proj(x) as one tcgen05 GEMM with the norms and rotation in its epilogue."""
+    _require_cuda("x", x, torch.bfloat16)
+    _require_cuda("w_qkv", w_qkv, torch.bfloat16)
+    if x.dim() != 3:
+        raise ValueError("x must be (B, S, K)")
+    B, S, K = x.shape
+    if x.stride(2) != 1 or (B > 1 and x.stride(0) != S * x.stride(1)):
+        raise ValueError("x rows must have a contiguous last dim and be evenly strided across the batch")
+    xf = x.as_strided((B * S, K), (x.stride(1), 1))
+    nh = n_q + 2 * n_k
+    if w_qkv.dim() != 2 or w_qkv.stride(1) != 1 or w_qkv.shape != (nh * 128, K):
+        raise ValueError(f"w_qkv must be ({nh * 128}, {K}) with a contiguous last dim")
+    for nm, t in (("q_norm_w", q_norm_w), ("k_norm_w", k_norm_w)):
+        _require_cuda(nm, t, torch.bfloat16)
+        if t.shape != (128,) or not t.is_contiguous():
+            raise ValueError(f"{nm} must be a contiguous (128,) tensor")
+    for nm, t in (("cos", cos), ("sin", sin)):
+        _require_cuda(nm, t, torch.bfloat16)
+        if t.shape != (B, S, 128) or t.stride(-1) != 1:
+            raise ValueError(f"{nm} must be (B, S, 128) with a contiguous last dim")
+    if cos.stride() != sin.stride():
+        raise ValueError("cos and sin must share strides")
+    out = torch.empty(B, S, nh, 128, dtype=torch.bfloat16, device=x.device)
+    L = _lib.lib()
+    with _device_ctx(x):
+        _lib.check_launch(L.tg_gemm_qkv_rope(xf.data_ptr(), xf.stride(0), w_qkv.data_ptr(), w_qkv.stride(0),
+                                             out.data_ptr(), nh * 128, B * S, K, n_q, n_k, q_norm_w.data_ptr(),
+                                             k_norm_w.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+                                             cos.stride(1), S, float(eps), _stream(x)))
+    return out
+
+
 def device_error(clear: bool = False) -> int:
     """Flags recorded by kernels whose bounded waits gave up on the current device (synchronises)."""
     return _lib.device_error(torch.cuda.current_stream().cuda_stream, clear)
