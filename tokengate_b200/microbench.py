@@ -120,11 +120,13 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
     epilogue at hidden 2048, intermediate 6144 and M = 2768 (Phase 2) and
     32768 (Phase 1) rows: TFLOP/s of 2*M*2048*12288, beside cuBLAS's bf16
     GEMM into [gate | up] alone and with the silu_mul kernel after it (the
-    chain it replaces)."""
+    chain it replaces). gemm_qkv_rope: the attention input projection with
+    the q/k RMSNorm + RoPE epilogue at hidden 2048, 16/8 heads, the same row
+    counts, beside cuBLAS's GEMM into [q | k | v] with qk_norm_rope after it."""
     g = torch.Generator(device=dev).manual_seed(0)
     flush = _L2Flush(dev)
     out = {"timing": f"CUDA events, median of {iters} launches, L2 flushed (a 256 MB read) before each",
-           "attention": [], "gate_score": [], "topk": [], "gather": [], "gemm_swiglu": []}
+           "attention": [], "gate_score": [], "topk": [], "gather": [], "gemm_swiglu": [], "gemm_qkv_rope": []}
     for S, kind in ((4096, "per-key bias"), (2768, "Phase-2 bias row"), (8192, "no bias"), (32768, "no bias")):
         q = torch.randn(1, S, 16, 128, device=dev, dtype=torch.bfloat16, generator=g)
         k = torch.randn(1, S, 8, 128, device=dev, dtype=torch.bfloat16, generator=g)
@@ -185,6 +187,25 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
                                        cublas_gemm_us=ms_lin * 1e3, cublas_gemm_tflops=tf_lin,
                                        vs_cublas_gemm=tf / tf_lin, cublas_plus_silu_mul_us=(ms_lin + ms_silu) * 1e3))
         del x, gu
+    nq, nk = 16, 8
+    nh = nq + 2 * nk
+    w = (torch.randn(nh * 128, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(128, device=dev, generator=g)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(128, device=dev, generator=g)).to(torch.bfloat16)
+    for M in (2768, 32768):
+        x = torch.randn(1, M, K, device=dev, dtype=torch.bfloat16, generator=g)
+        ang = torch.rand(1, M, 128, device=dev, generator=g) * 6
+        cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+        flops = 2.0 * M * K * nh * 128
+        ms = _time_flushed(lambda: ops.gemm_qkv_rope(x, w, nq, nk, qw, kw, cos, sin, 1e-6), flush, iters)
+        ms_lin = _time_flushed(lambda: torch.nn.functional.linear(x, w), flush, iters)
+        qkv = torch.nn.functional.linear(x, w).view(1, M, nh, 128)
+        ms_rope = _time_flushed(lambda: ops.qk_norm_rope(qkv[:, :, :nq], qkv[:, :, nq:nq + nk], qw, kw, cos, sin,
+                                                          1e-6), flush, iters)
+        tf = flops / ms / 1e9
+        out["gemm_qkv_rope"].append(dict(rows=M, K=K, heads="16/8", us=ms * 1e3, tflops=tf, frac=tf / tflops_peak,
+                                         cublas_gemm_us=ms_lin * 1e3, cublas_plus_qk_norm_rope_us=(ms_lin + ms_rope) * 1e3))
+        del x, qkv
     assert ops.device_error() == 0
     return out
 
