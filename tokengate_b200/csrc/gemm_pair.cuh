@@ -70,7 +70,8 @@ struct GemmLayout {
   static constexpr int kSmCos = kStages * kGsStageBytes;
   static constexpr int kSmSin = kSmCos + (kRope ? 128 * kCsRow : 0);
   static constexpr int kSmGain = kSmSin + (kRope ? 128 * kCsRow : 0);  // q gains, then k gains
-  static constexpr int kSmBar = kSmGain + (kRope ? 512 : 0);
+  static constexpr int kSmStage = kSmGain + (kRope ? 512 : 0);  // 8 epilogue warps x 2 KB
+  static constexpr int kSmBar = kSmStage + 8 * 2048;
   // barriers
   static constexpr int kFull = 0;                   // rank 0, stages: both CTAs' A and B bytes
   static constexpr int kEmpty = kFull + kStages;    // both, stages: the stage's MMAs done
@@ -121,6 +122,29 @@ __device__ __forceinline__ float swiglu_bf16(float g_acc, float u_acc) {
   return a * u;
 }
 
+// Writes 32 consecutive bf16 of each of a warp's 32 rows (lane = row, vals =
+// its 16 packed pairs) to gbase + row*ld: the warp transposes them through
+// its 2 KB of shared memory (16-byte chunks XOR-swizzled by row so both
+// passes take 4 wavefronts) so that each store instruction writes 64
+// contiguous bytes of 8 rows instead of 16 bytes of 32 rows. Rows >= nvalid
+// are not written.
+__device__ __forceinline__ void store_rows_coalesced(const uint32_t (&vals)[16], uint8_t* stage,
+                                                     __nv_bfloat16* gbase, int64_t ld, int nvalid, int lane) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    *reinterpret_cast<uint4*>(stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(vals[4 * k], vals[4 * k + 1], vals[4 * k + 2], vals[4 * k + 3]);
+  __syncwarp();
+  const int k = lane & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int rr = (lane >> 2) + 8 * i;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4));
+    if (rr < nvalid) *reinterpret_cast<uint4*>(gbase + rr * ld + k * 8) = v;
+  }
+  __syncwarp();  // the buffer is rewritten by the next call
+}
+
 // The q/k/v epilogue of one row and one head (128 TMEM columns at tcol).
 // q/k heads: x = bf16(acc); y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w);
 // out[d] = bf16(bf16(y[d] cos[d]) + bf16(-y[d+64] sin[d])),
@@ -128,23 +152,20 @@ __device__ __forceinline__ float swiglu_bf16(float g_acc, float u_acc) {
 // (Qwen3RMSNorm and apply_rotary_pos_emb with rotate_half, as qk_finish in
 // layer_glue.cuh rounds them), with the row's cos / sin and the gains read
 // from shared memory. v heads: bf16(acc).
+// gbase: the head's column 0 in the warp's first row; nvalid: rows of the
+// warp's 32 below M.
 __device__ __forceinline__ void qkv_rope_head(const GemmPairParams& p, uint32_t tcol, int hd,
                                               const uint8_t* cosr, const uint8_t* sinr, const uint8_t* gain,
-                                              __nv_bfloat16* orow, bool valid) {
+                                              uint8_t* stage, __nv_bfloat16* gbase, int nvalid, int lane) {
   if (hd >= p.n_q + p.n_k) {
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
       uint32_t v[32];
       tmem_ld32(tcol + c * 32, v);
-      uint4 w[4];
-      uint32_t* wp = reinterpret_cast<uint32_t*>(w);
+      uint32_t w[16];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) wp[e] = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
-      if (valid) {
-        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) dst[e] = w[e];
-      }
+      for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
+      store_rows_coalesced(w, stage, gbase + c * 32, p.ld_out, nvalid, lane);
     }
     return;
   }
@@ -209,15 +230,8 @@ __device__ __forceinline__ void qkv_rope_head(const GemmPairParams& p, uint32_t 
         ob[q8 * 4 + e] = pack_bf16x2(qc0 + qs0, qc1 + qs1);
       }
     }
-    if (valid) {
-      uint4* da = reinterpret_cast<uint4*>(orow + c * 32);
-      uint4* db = reinterpret_cast<uint4*>(orow + 64 + c * 32);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        da[e] = make_uint4(oa[4 * e], oa[4 * e + 1], oa[4 * e + 2], oa[4 * e + 3]);
-        db[e] = make_uint4(ob[4 * e], ob[4 * e + 1], ob[4 * e + 2], ob[4 * e + 3]);
-      }
-    }
+    store_rows_coalesced(oa, stage, gbase + c * 32, p.ld_out, nvalid, lane);
+    store_rows_coalesced(ob, stage, gbase + 64 + c * 32, p.ld_out, nvalid, lane);
   }
 }
 
@@ -362,8 +376,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
     for (int t = cid; t < p.n_tiles; t += n_clusters, ++it) {
       const int buf = it & 1;
       const int mt = t / p.n_tiles_n, nt = t - mt * p.n_tiles_n;
-      const int64_t row = (int64_t)mt * 256 + (int)rank * 128 + r;
-      const bool valid = row < p.M;
+      const int64_t row0 = (int64_t)mt * 256 + (int)rank * 128 + sub * 32;  // the warp's first row
+      const int64_t left = (int64_t)p.M - row0;
+      const int nvalid = left <= 0 ? 0 : (left >= 32 ? 32 : (int)left);
+      uint8_t* stage = smem + Lay::kSmStage + warp * 2048;
       // q/k tiles: stage this CTA's 128 rotary cos / sin rows (4096 16-byte
       // chunks, 16 per thread, coalesced along each row) while the
       // accumulator is still being computed
@@ -400,24 +416,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
           uint32_t g[32], u[32];
           tmem_ld32(tacc + c * 32, g);
           tmem_ld32(tacc + 128 + c * 32, u);
-          uint4 w[4];
-          uint32_t* wp = reinterpret_cast<uint32_t*>(w);
+          uint32_t wv[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e)
-            wp[e] = pack_bf16x2(swiglu_bf16(__uint_as_float(g[2 * e]), __uint_as_float(u[2 * e])),
+            wv[e] = pack_bf16x2(swiglu_bf16(__uint_as_float(g[2 * e]), __uint_as_float(u[2 * e])),
                                 swiglu_bf16(__uint_as_float(g[2 * e + 1]), __uint_as_float(u[2 * e + 1])));
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(p.out + row * p.ld_out + col0 + c * 32);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) dst[e] = w[e];
-          }
+          store_rows_coalesced(wv, stage, p.out + row0 * p.ld_out + col0 + c * 32, p.ld_out, nvalid, lane);
         }
       } else {
         const int hd = 2 * nt + half;
         if (hd < p.n_heads)
           qkv_rope_head(p, tmem + lane_off + (uint32_t)buf * 256u + (uint32_t)half * 128u, hd,
                         smem + Lay::kSmCos + r * Lay::kCsRow, smem + Lay::kSmSin + r * Lay::kCsRow,
-                        smem + Lay::kSmGain, p.out + row * p.ld_out + (int64_t)hd * 128, valid);
+                        smem + Lay::kSmGain, stage, p.out + row0 * p.ld_out + (int64_t)hd * 128, nvalid, lane);
         if (rope) {
           // this warp no longer reads the staged rows
           __syncwarp();
