@@ -213,7 +213,7 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=("attn", "score", "topk", "gather", "branch", "tables", "decode",
-                                       "generate", "gemv", "gemvchain", "gemm"))
+                                       "generate", "gemv", "gemvchain", "gemm", "qkv"))
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--new", type=int, default=64)
     ap.add_argument("--gate", default="linear", choices=("linear", "e2e"))
@@ -258,6 +258,26 @@ def main(argv=None):
         flops = 2.0 * M * K * 2 * I
         res.update(rows=M, k=K, inter=I, ms=ms, us=ms * 1e3, tflops=flops / ms / 1e9,
                    cublas_us=ms_ref * 1e3, cublas_tflops=flops / ms_ref / 1e9)
+    elif a.kernel == "qkv":
+        # the attention input projection with the q/k RMSNorm + RoPE epilogue:
+        # --seq rows, --hidden K, --hq / --hkv heads; cuBLAS + qk_norm_rope beside it
+        M, K, nq, nk = S, a.hidden, a.hq, a.hkv
+        nh = nq + 2 * nk
+        x = torch.randn(1, M, K, device=dev, dtype=torch.bfloat16, generator=g)
+        w = (torch.randn(nh * 128, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+        qw = (1 + 0.1 * torch.randn(128, device=dev, generator=g)).to(torch.bfloat16)
+        ang = torch.rand(1, M, 128, device=dev, generator=g) * 6
+        cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+        ms = _graph_time(lambda: ops.gemm_qkv_rope(x, w, nq, nk, qw, qw, cos, sin, 1e-6), 3, a.iters)
+        qkv = torch.nn.functional.linear(x, w).view(1, M, nh, 128)
+
+        def eager():
+            torch.nn.functional.linear(x, w, out=qkv.view(1, M, nh * 128))
+            ops.qk_norm_rope(qkv[:, :, :nq], qkv[:, :, nq:nq + nk], qw, qw, cos, sin, 1e-6)
+        ms_ref = _graph_time(eager, 3, a.iters)
+        flops = 2.0 * M * K * nh * 128
+        res.update(rows=M, k=K, heads=f"{nq}/{nk}", ms=ms, us=ms * 1e3, tflops=flops / ms / 1e9,
+                   cublas_plus_qk_norm_rope_us=ms_ref * 1e3)
     elif a.kernel == "gemv":
         x = torch.randn(B, a.hidden, device=dev, dtype=torch.bfloat16, generator=g)
         w = (torch.randn(a.n, a.hidden, device=dev, generator=g) / a.hidden ** 0.5).to(torch.bfloat16)
