@@ -381,8 +381,9 @@ int tg_decode_attn_workspace(int B, int Hq, int n_keys, size_t* bytes);
  * GPU that loads it, until the process exits. Nothing is allocated. A
  * problem needing more than 8 MiB of scratch (B * Hq * ceil(n_keys / 128) *
  * 528 bytes) is rejected with TG_ERR_INVALID_ARGUMENT. The first call on a
- * device looks up the buffer's device address (make it before any stream
- * capture on that device). All calls share the one buffer: calls that
+ * device looks up the buffer's device address: make it before any stream
+ * capture on that device (a first call inside a capture returns
+ * TG_ERR_INVALID_ARGUMENT and leaves the capture intact). All calls share the one buffer: calls that
  * overlap on the GPU race and must be serialized by the caller. No
  * counterpart in the reference.
  */

@@ -8,9 +8,14 @@ second reusing the scratch the first left behind — bit for bit, and both
 against a float32 restatement of the decode math with the decode tests'
 tolerance (max-abs <= 1e-2, cosine >= 0.9999). Also: a cache of at most one
 key chunk (no partials, the scratch unused), a second device when there is
-one (its own scratch address), and that an oversized problem is refused.
+one (its own scratch address), that an oversized problem is refused, and
+that a device's first call inside a stream capture is refused cleanly.
 Kept in a file of its own, collected last."""
 import ctypes
+import os
+import subprocess
+import sys
+import textwrap
 
 import pytest
 import torch
@@ -111,3 +116,39 @@ def test_noalloc_decode_rejects_oversized(cuda):
     nv = torch.full((64,), 10240, dtype=torch.int32, device=cuda)
     with pytest.raises(TokenGateArgumentError, match="8388608-byte buffer"):
         _noalloc(q, k, k, bias, qs, nv, 10240, 10240)
+
+
+def test_noalloc_first_call_inside_capture_is_refused(cuda):
+    """A device's first call resolves the scratch address, which a stream
+    capture cannot record: inside a capture it must return
+    TG_ERR_INVALID_ARGUMENT without touching the capture; after one call
+    outside, calls inside a capture work. Run in a fresh process, so this
+    device has made no call yet."""
+    code = textwrap.dedent("""
+        import torch
+        import tests.test_zz_no_alloc as t
+        from tokengate_b200._lib import TokenGateArgumentError
+        dev = torch.device("cuda", 0)
+        q, k, v, bias, qs, n_valid = t._case(dev, 1, 16, 8, 300, 305, 9)
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        refused = False
+        with torch.cuda.graph(g, stream=s):
+            try:
+                t._noalloc(q, k, v, bias, qs, n_valid, 300, 305)
+            except TokenGateArgumentError as e:
+                refused = "before any stream capture" in str(e)
+        assert refused
+        ref = t._noalloc(q, k, v, bias, qs, n_valid, 300, 305)
+        torch.cuda.synchronize()
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=s):
+            out = t._noalloc(q, k, v, bias, qs, n_valid, 300, 305)
+        g2.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        print("NOALLOC_CAPTURE_OK")
+    """)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    res = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0 and "NOALLOC_CAPTURE_OK" in res.stdout, res.stdout[-2000:] + res.stderr[-2000:]

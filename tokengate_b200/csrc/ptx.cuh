@@ -320,7 +320,7 @@ __device__ __forceinline__ uint4 ld_nc_v4(const uint4* ptr) {
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
-  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));  // pure: free to schedule
   return y;
 }
 

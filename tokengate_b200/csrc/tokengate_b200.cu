@@ -1095,6 +1095,14 @@ int tg_decode_attn_noalloc(const void* q, int64_t q_sb, int64_t q_sh, const floa
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (g_noalloc_ptr[dev] == nullptr) {
+      // the scratch address is resolved on a device's first call, which a
+      // stream capture cannot record: refuse instead of invalidating it
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cs) == cudaSuccess &&
+          cs != cudaStreamCaptureStatusNone)
+        return fail(TG_ERR_INVALID_ARGUMENT,
+                    "decode_attn_noalloc: the first call on a device must come before any stream capture "
+                    "(it resolves the scratch buffer's address); make one call outside the capture first");
       void* ptr = nullptr;
       cudaError_t e = cudaGetSymbolAddress(&ptr, g_tg_noalloc_scratch);
       if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(decode scratch)");
