@@ -264,7 +264,10 @@ int tg_gemm_qkv_rope(const void* x, int64_t ld_x, const void* w_qkv, int64_t ld_
  *   computed in bf16 by CastLinear (e2e_gate_module.py:125-135) and returned
  *   as bf16 (gate_forward.py:521), then cast to the gate's fp32 (:1402-1405).
  * The dot product has a fixed order and silu uses IEEE operations only, so the
- * result is reproducible bit for bit; -0 is stored as +0.
+ * result is reproducible bit for bit; -0 is stored as +0. bf16(silu(g)) is
+ * read from a table of all 65536 bf16 patterns held in the library's device
+ * memory (128 KB per device), which each call rewrites on `stream` before its
+ * readout: overlapping calls on different streams write the same values.
  *
  * gu: bf16 (B, S, >= 2*inter), strides (gu_sb, gu_ss, 1), rows 16-byte aligned;
  * inter a multiple of 256. w_row: bf16 (inter,), 16-byte aligned.

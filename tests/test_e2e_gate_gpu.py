@@ -80,6 +80,31 @@ def test_branch_score_bit_exact(cuda, inter):
     assert not (out.cpu().numpy().view(np.uint32) == 0x80000000).any()     # no -0
 
 
+def test_branch_score_every_gate_pattern(cuda):
+    """Every bf16 gate pattern (inf and NaN included), one per row: row r holds
+    pattern r at column r % 16 with u = 1 there and 0 elsewhere, w = 1 on the
+    first 16 columns, so the score is the row's bf16(silu(g)) itself. Bit-exact
+    against the oracle's IEEE SiLU (NaN patterns: NaN on both sides)."""
+    inter = 256
+    n = 1 << 16
+    r = torch.arange(n, device=cuda)
+    col = r % 16
+    g_bits = torch.zeros(n, inter, dtype=torch.int32, device=cuda)
+    g_bits[r, col] = torch.where(r >= 32768, r - 65536, r).to(torch.int32)   # int16 range
+    g = g_bits.to(torch.int16).view(torch.bfloat16)
+    u = torch.zeros(n, inter, dtype=torch.bfloat16, device=cuda)
+    u[r, col] = 1.0
+    gu = torch.cat([g, u], dim=1).unsqueeze(0).contiguous()
+    w = torch.zeros(inter, dtype=torch.bfloat16, device=cuda)
+    w[:16] = 1.0
+    out = ops.branch_score(gu, w, [0], [n])[0].cpu().numpy()
+    ref = ge.branch_score(_bits(gu[0]), _bits(w))
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(out), nan)
+    assert np.array_equal(out[~nan].view(np.uint32), ref[~nan].view(np.uint32))
+    assert nan.sum() == 2 * 127 + 1             # the NaN patterns and silu(-inf) = -inf / inf
+
+
 def test_branch_score_vs_reference_fixture(cuda):
     z = np.load(os.path.join(GOLD, "e2e_gate.npz"))
     gu = torch.from_numpy(z["gu"].view(np.int16)).view(torch.bfloat16).to(cuda).unsqueeze(0)

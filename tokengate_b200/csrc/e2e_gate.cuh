@@ -16,7 +16,11 @@
 //   accumulator from 0; the 32 partials are combined by the xor butterfly
 //   (16, 8, 4, 2, 1); silu(g) = g / (1 + exp(-g)) with IEEE division and the
 //   IEEE-only tg_exp below; the bf16 result is stored as fp32 with -0
-//   replaced by +0 (the selection score compares them equal).
+//   replaced by +0 (the selection score compares them equal). bf16(silu(g))
+//   is read from a 65536-entry table of that same function over all bf16
+//   patterns (built on the stream before each readout, staged per CTA in
+//   shared memory), which takes the SiLU's ~30 instructions per element off
+//   the issue path of an otherwise HBM-bound pass.
 //
 // phase2_tables_kernel — everything between the raw score and the attention
 //   kernel's operands, for all Phase-2 layers in one launch:
@@ -98,7 +102,41 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
-__global__ void __launch_bounds__(256) branch_score_kernel(const BranchParams p) {
+// bf16(silu(g)) for every bf16 bit pattern g: the branch's activation takes
+// only 2^16 values, so the IEEE-only SiLU is evaluated once per pattern
+// (silu_lut_kernel, on the launching stream before every readout) and the
+// readout looks it up in shared memory. Entry g holds the bf16 bits of
+// bf16_round(tg_silu(g)), i.e. exactly the value the per-element evaluation
+// produced, NaN patterns included.
+constexpr int kSiluLutEntries = 1 << 16;
+constexpr int kSiluLutBytes = kSiluLutEntries * 2;
+constexpr int kBranchThreads = 1024;
+__device__ __align__(16) uint16_t g_silu_bf16_lut[kSiluLutEntries];
+
+__global__ void __launch_bounds__(256) silu_lut_kernel() {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;  // the grid covers 2^16 exactly
+  g_silu_bf16_lut[i] = __bfloat16_as_ushort(__float2bfloat16_rn(tg_silu(__uint_as_float(i << 16))));
+}
+
+// act = bf16(bf16(silu(g)) * u) for the two bf16 lanes of a packed word; the
+// activations of the low and high halves go to a0 / a1.
+__device__ __forceinline__ void branch_act2(const uint16_t* lut, uint32_t gw, uint32_t uw, float& a0,
+                                            float& a1) {
+  const float s0 = __uint_as_float((uint32_t)lut[gw & 0xFFFFu] << 16);
+  const float s1 = __uint_as_float((uint32_t)lut[gw >> 16] << 16);
+  a0 = bf16_round(__fmul_rn(s0, __uint_as_float(uw << 16)));
+  a1 = bf16_round(__fmul_rn(s1, __uint_as_float(uw & 0xFFFF0000u)));
+}
+
+// One CTA per SM (the table fills 128 KB of shared memory), one warp per row.
+__global__ void __launch_bounds__(kBranchThreads, 1) branch_score_kernel(const BranchParams p) {
+  extern __shared__ __align__(16) uint16_t s_lut[];
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(g_silu_bf16_lut);
+    uint4* dst = reinterpret_cast<uint4*>(s_lut);
+    for (int i = threadIdx.x; i < kSiluLutBytes / 16; i += kBranchThreads) dst[i] = src[i];
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int nv = p.inter >> 8;  // 8-element vectors per lane
@@ -128,11 +166,9 @@ __global__ void __launch_bounds__(256) branch_score_kernel(const BranchParams p)
         const uint32_t* ww = reinterpret_cast<const uint32_t*>(&w4);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float a0 = bf16_round(__fmul_rn(bf16_round(tg_silu(__uint_as_float(gw[e] << 16))),
-                                                __uint_as_float(uw[e] << 16)));
+          float a0, a1;
+          branch_act2(s_lut, gw[e], uw[e], a0, a1);
           acc = __fmaf_rn(a0, __uint_as_float(ww[e] << 16), acc);
-          const float a1 = bf16_round(__fmul_rn(bf16_round(tg_silu(__uint_as_float(gw[e] & 0xFFFF0000u))),
-                                                __uint_as_float(uw[e] & 0xFFFF0000u)));
           acc = __fmaf_rn(a1, __uint_as_float(ww[e] & 0xFFFF0000u), acc);
         }
       }
@@ -144,11 +180,9 @@ __global__ void __launch_bounds__(256) branch_score_kernel(const BranchParams p)
       const uint32_t* ww = reinterpret_cast<const uint32_t*>(&w4);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float a0 = bf16_round(__fmul_rn(bf16_round(tg_silu(__uint_as_float(gw[e] << 16))),
-                                              __uint_as_float(uw[e] << 16)));
+        float a0, a1;
+        branch_act2(s_lut, gw[e], uw[e], a0, a1);
         acc = __fmaf_rn(a0, __uint_as_float(ww[e] << 16), acc);
-        const float a1 = bf16_round(__fmul_rn(bf16_round(tg_silu(__uint_as_float(gw[e] & 0xFFFF0000u))),
-                                              __uint_as_float(uw[e] & 0xFFFF0000u)));
         acc = __fmaf_rn(a1, __uint_as_float(ww[e] & 0xFFFF0000u), acc);
       }
     }

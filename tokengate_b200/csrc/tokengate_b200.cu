@@ -811,6 +811,23 @@ int tg_branch_score(const void* gu, int64_t gu_sb, int64_t gu_ss, int inter, con
       (gu_sb & 7))
     return fail(TG_ERR_ALIGNMENT, "branch_score: rows and w_row must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int64_t all_rows = 0;
+  for (int b = 0; b < B; ++b) {
+    if (row_begin[b] < 0 || row_count[b] < 0)
+      return fail(TG_ERR_INVALID_ARGUMENT, "branch_score: negative row range for request %d", b);
+    all_rows += row_count[b];
+  }
+  if (all_rows == 0) return TG_OK;
+  int dev, st;
+  if ((st = current_device(&dev))) return st;
+  static bool attr_set[kMaxDevices] = {};
+  cudaError_t ea = smem_limit_once(tg::branch_score_kernel, tg::kSiluLutBytes, attr_set, dev);
+  if (ea != cudaSuccess) return cuda_fail(ea, "cudaFuncSetAttribute(branch_score smem)");
+  // the SiLU table, rebuilt on this stream (2^16 evaluations) so that every
+  // readout, captured or not, finds it complete
+  tg::silu_lut_kernel<<<tg::kSiluLutEntries / 256, 256, 0, s>>>();
+  ea = cudaGetLastError();
+  if (ea != cudaSuccess) return cuda_fail(ea, "silu_lut launch");
   for (int b0 = 0; b0 < B; b0 += tg::kBranchMaxReq) {
     const int nb = B - b0 < tg::kBranchMaxReq ? B - b0 : tg::kBranchMaxReq;
     tg::BranchParams p;
@@ -825,15 +842,13 @@ int tg_branch_score(const void* gu, int64_t gu_sb, int64_t gu_ss, int inter, con
     p.B = nb;
     p.row_off[0] = 0;
     for (int i = 0; i < nb; ++i) {
-      if (row_begin[b0 + i] < 0 || row_count[b0 + i] < 0)
-        return fail(TG_ERR_INVALID_ARGUMENT, "branch_score: negative row range for request %d", b0 + i);
       p.begin[i] = row_begin[b0 + i];
       p.row_off[i + 1] = p.row_off[i] + row_count[b0 + i];
     }
     p.total_rows = p.row_off[nb];
     if (p.total_rows == 0) continue;
-    const int64_t blocks = resident_blocks((p.total_rows + 7) / 8, 4);  // 62 registers: 4 CTAs per SM
-    tg::branch_score_kernel<<<(unsigned)blocks, 256, 0, s>>>(p);
+    const int64_t blocks = resident_blocks((p.total_rows + 31) / 32, 1);  // 32 rows per CTA at a time
+    tg::branch_score_kernel<<<(unsigned)blocks, tg::kBranchThreads, tg::kSiluLutBytes, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "branch_score launch");
   }
