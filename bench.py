@@ -32,8 +32,9 @@ Reported (one JSON line from rank 0):
                ranks, static batches of 8, K=2000: aggregate tokens/s, p50
                TTFT, per-GPU TTFT spread and the slowest GPU's makespan;
   gpu_ops      (N=1) single-kernel figures at the benchmarked shapes: attention
-               TFLOP/s at S = 4096 / 2768 / 8192 / 32768, gate score, top-K
-               and gather GB/s for 1 and 8 requests (microbench.ops_table);
+               TFLOP/s at S = 4096 / 2768 / 8192 / 32768, gate score, top-K,
+               gather and finalized-gate readout GB/s for 1 and 8 requests,
+               the fused projections beside cuBLAS (microbench.ops_table);
   cpu_baseline (N=1) the CPU oracle's gated prefill (float32 torch, all host
                threads) at the same config, timed by parts (one Phase-1 layer
                on 32768 tokens, the selection, one Phase-2 layer, the head)

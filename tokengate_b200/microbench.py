@@ -116,7 +116,10 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
     (score: the bf16 state rows + w + fp32 scores; top-K: scores read +
     kept positions and bias row written; gather: the hidden rows and the K/V
     rows of two below-gate layers, read and written) and the fraction of
-    `hbm_peak_gbs`. gemm_swiglu: the MLP up-projection with the SwiGLU
+    `hbm_peak_gbs`. branch_score: the finalized gate's readout over the same
+    state rows' bf16 [gate | up] projections (inter 6144), GB/s of those rows
+    + the readout row + fp32 scores (the SiLU table build included in the
+    time). gemm_swiglu: the MLP up-projection with the SwiGLU
     epilogue at hidden 2048, intermediate 6144 and M = 2768 (Phase 2) and
     32768 (Phase 1) rows: TFLOP/s of 2*M*2048*12288, beside cuBLAS's bf16
     GEMM into [gate | up] alone and with the silu_mul kernel after it (the
@@ -126,7 +129,8 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
     g = torch.Generator(device=dev).manual_seed(0)
     flush = _L2Flush(dev)
     out = {"timing": f"CUDA events, median of {iters} launches, L2 flushed (a 256 MB read) before each",
-           "attention": [], "gate_score": [], "topk": [], "gather": [], "gemm_swiglu": [], "gemm_qkv_rope": []}
+           "attention": [], "gate_score": [], "topk": [], "gather": [], "branch_score": [], "gemm_swiglu": [],
+           "gemm_qkv_rope": []}
     for S, kind in ((4096, "per-key bias"), (2768, "Phase-2 bias row"), (8192, "no bias"), (32768, "no bias")):
         q = torch.randn(1, S, 16, 128, device=dev, dtype=torch.bfloat16, generator=g)
         k = torch.randn(1, S, 8, 128, device=dev, dtype=torch.bfloat16, generator=g)
@@ -173,6 +177,14 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
         out["gather"].append(dict(requests=B, k=K, us=ms * 1e3, gbs=byts / ms / 1e6,
                                   frac=byts / ms / 1e6 / hbm_peak_gbs))
         del h, kv, dh, dkv
+        gu = torch.randn(B, n_art, 2 * 6144, device=dev, dtype=torch.bfloat16, generator=g)
+        wr = (torch.randn(6144, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        bs = ops.branch_score(gu, wr, [0] * B, [n_art] * B)
+        ms = _time_flushed(lambda: ops.branch_score(gu, wr, [0] * B, [n_art] * B, out=bs), flush, iters)
+        byts = B * n_art * (4 * 6144 + 4) + 2 * 6144
+        out["branch_score"].append(dict(requests=B, inter=6144, us=ms * 1e3, gbs=byts / ms / 1e6,
+                                        frac=byts / ms / 1e6 / hbm_peak_gbs))
+        del gu, bs
     K, inter = 2048, 6144
     w = (torch.randn(2 * inter, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
     for M in (2768, 32768):
