@@ -86,29 +86,35 @@ def _phase2_bias_row(n_kept: int, n_alloc: int, g) -> torch.Tensor:
     return b.to(torch.bfloat16).float()
 
 
-def test_phase2_attention_2768_per_key(cuda):
+# B=1 is the bench's Phase-2 launch: its three heaviest row blocks (rows 2432
+# and up) run one head per CTA; at B=2 every CTA takes a head pair.
+@pytest.mark.parametrize("B", [1, 2])
+def test_phase2_attention_2768_per_key(cuda, B):
     """The linear gate's Phase 2: (B, 1, n_alloc) bias row; request 1 is 68 rows shorter (pads)."""
-    B, S, Hq, Hkv = 2, 2768, 16, 8
+    S, Hq, Hkv = 2768, 16, 8
     g = torch.Generator().manual_seed(2768)
-    q = torch.randn(B, S, Hq, 128, generator=g).to(torch.bfloat16).to(cuda)
-    k = torch.randn(B, S, Hkv, 128, generator=g).to(torch.bfloat16).to(cuda)
-    v = torch.randn(B, S, Hkv, 128, generator=g).to(torch.bfloat16).to(cuda)
-    bias = torch.stack([_phase2_bias_row(2768, S, g), _phase2_bias_row(2700, S, g)]).view(B, 1, S)
-    rows = np.unique(np.r_[0:4, 127:130, 511:514, 1400:1403, 2511:2514, 2640:2768:3, 2699, 2700, 2767])
+    q = torch.randn(2, S, Hq, 128, generator=g).to(torch.bfloat16)[:B].to(cuda)
+    k = torch.randn(2, S, Hkv, 128, generator=g).to(torch.bfloat16)[:B].to(cuda)
+    v = torch.randn(2, S, Hkv, 128, generator=g).to(torch.bfloat16)[:B].to(cuda)
+    bias = torch.stack([_phase2_bias_row(2768, S, g), _phase2_bias_row(2700, S, g)])[:B].view(B, 1, S)
+    rows = np.unique(np.r_[0:4, 127:130, 511:514, 1400:1403, 2432:2560:7, 2511:2514, 2640:2768:3, 2699, 2700,
+                           2767])
     _check_attn(q, k, v, bias.to(cuda), causal=True, rows=rows)
 
 
-def test_phase2_attention_2768_per_head_qscale(cuda):
+@pytest.mark.parametrize("B", [1, 2])
+def test_phase2_attention_2768_per_head_qscale(cuda, B):
     """The finalized gate's Phase 2: per-head bias (B, Hq, n_alloc) with -1e9
     pads and the scaled-softmax query scale (B, Hq, n_alloc)."""
-    B, S, Hq, Hkv = 2, 2768, 16, 8
+    S, Hq, Hkv = 2768, 16, 8
     g = torch.Generator().manual_seed(2769)
-    q = torch.randn(B, S, Hq, 128, generator=g).to(torch.bfloat16).to(cuda)
-    k = torch.randn(B, S, Hkv, 128, generator=g).to(torch.bfloat16).to(cuda)
-    v = torch.randn(B, S, Hkv, 128, generator=g).to(torch.bfloat16).to(cuda)
-    bias = (torch.randn(B, Hq, S, generator=g) * 2).to(torch.bfloat16).float()
+    q = torch.randn(2, S, Hq, 128, generator=g).to(torch.bfloat16)[:B].to(cuda)
+    k = torch.randn(2, S, Hkv, 128, generator=g).to(torch.bfloat16)[:B].to(cuda)
+    v = torch.randn(2, S, Hkv, 128, generator=g).to(torch.bfloat16)[:B].to(cuda)
+    bias = (torch.randn(2, Hq, S, generator=g) * 2).to(torch.bfloat16).float()
     bias[1, :, 2700:] = -1e9
-    qrs = (0.8 + 0.6 * torch.rand(B, Hq, S, generator=g))
+    qrs = (0.8 + 0.6 * torch.rand(2, Hq, S, generator=g))
+    bias, qrs = bias[:B].contiguous(), qrs[:B].contiguous()
     rows = np.unique(np.r_[0:3, 127:130, 1000:1003, 2000:2768:5, 2767])
     _check_attn(q, k, v, bias.to(cuda), causal=True, rows=rows, qrs=qrs.to(cuda))
 

@@ -7,7 +7,10 @@
 //
 //  * one CTA owns TWO 128-row query tiles that share one KV head: two heads
 //    of a GQA group at the same rows (Hq/Hkv even), or two consecutive row
-//    blocks of one head otherwise. K/V tiles are loaded once for both.
+//    blocks of one head otherwise. K/V tiles are loaded once for both. In a
+//    launch of about one wave the heaviest row blocks run one head per CTA
+//    (tile 1 unused): those CTAs are the launch's span, and one tile's key
+//    block costs ~1.8 us against ~2.0 for two.
 //  * the key bias rides in the QK product: each K tile gets a 16-column
 //    extension [b0_hi, b0_lo, b1_hi, b1_lo, 0...] (bias / scale split into two
 //    bf16 that sum to it to ~16 bits) and each Q tile a constant one-hot
@@ -115,6 +118,7 @@ struct AttnParams {
   int n_mblocks;   // ceil(Sq / 128)
   int n_kblocks;   // ceil(Sk / 128)
   int heads_per_unit_row;  // pair_heads ? Hq/2 : Hq
+  int n_single_rows;       // pair_heads: the heaviest row blocks run one head per CTA
   float scale;             // softmax_scale
   float scale_log2;        // softmax_scale * log2(e)
   unsigned int* err;
@@ -126,15 +130,34 @@ struct TileInfo {
   int nblk;  // key blocks this tile needs (0 = tile unused)
 };
 
+// Work unit of this CTA. Units are numbered heavy rows first. With head
+// pairs, the first n_single_rows * Hq units are the last n_single_rows row
+// blocks, one head each (tile 1 unused), and the rest the other row blocks,
+// two heads each: splitting the longest units shortens the launch's tail when
+// it runs in about one wave.
 __device__ __forceinline__ void attn_unit(const AttnParams& p, TileInfo (&ti)[2]) {
-  const int u = blockIdx.x;
+  int u = blockIdx.x;
+  bool single = false;
   if (p.pair_heads) {
-    const int hp = u % p.heads_per_unit_row;
-    const int mb = p.n_mblocks - 1 - u / p.heads_per_unit_row;  // heavy rows first
+    const int n_single = p.n_single_rows * p.Hq;
+    if (u < n_single) {
+      single = true;
+      const int h = u % p.Hq;
+      const int mb = p.n_mblocks - 1 - u / p.Hq;
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      ti[t].head = 2 * hp + t;
-      ti[t].m0 = mb * kAttnBM;
+      for (int t = 0; t < 2; ++t) {
+        ti[t].head = h;
+        ti[t].m0 = mb * kAttnBM;
+      }
+    } else {
+      u -= n_single;
+      const int hp = u % p.heads_per_unit_row;
+      const int mb = p.n_mblocks - p.n_single_rows - 1 - u / p.heads_per_unit_row;  // heavy rows first
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        ti[t].head = 2 * hp + t;
+        ti[t].m0 = mb * kAttnBM;
+      }
     }
   } else {
     const int h = u % p.heads_per_unit_row;
@@ -156,6 +179,7 @@ __device__ __forceinline__ void attn_unit(const AttnParams& p, TileInfo (&ti)[2]
       ti[t].nblk = p.n_kblocks;
     }
   }
+  if (single) ti[1].nblk = 0;
 }
 
 // all lanes wait; the result is made warp-uniform

@@ -8,7 +8,12 @@
 #include <cstdio>
 #include <cstring>
 #include <cstdarg>
+#include <functional>
+#include <map>
 #include <mutex>
+#include <queue>
+#include <tuple>
+#include <vector>
 
 #include "../../include/tokengate_b200.h"
 #include "ptx.cuh"
@@ -256,6 +261,60 @@ int launch_gemm_pair(const void* x, int64_t ld_x, const void* w, int64_t w_rows,
   if (e != cudaSuccess) return cuda_fail(e, name);
   return TG_OK;
 }
+
+// How many of the heaviest row blocks of a causal head-pair launch run one
+// head per CTA. A list-scheduling model of the launch: CTAs go out in unit
+// order (batch-major as the grid is) to the SM that frees first, one CTA per
+// SM, and a CTA costs kFix + key blocks * (kPair for two heads, kSingle for
+// one), in microseconds: kFix and kPair from a global-timer trace of the
+// S=2768 launch, kSingle fitted to launches with 0..8 single-head rows
+// (S=2768: 51, 51, 49, 47, 48, 51, 55, 62 us; S=4096: 0 rows fastest). The
+// smallest count within 0.5 % of the shortest modelled span wins; launches
+// of more than two waves of head pairs keep 0 (their tail is a small share).
+// Memoised per shape.
+int attn_single_rows(int n_mblocks, int Hq, int B, int sms) {
+  constexpr double kFix = 5.3, kPair = 2.0, kSingle = 1.8;
+  const int64_t pair_ctas = (int64_t)n_mblocks * (Hq / 2) * B;
+  if (n_mblocks < 2 || pair_ctas > 2LL * sms) return 0;
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int>, int> memo;
+  const auto key = std::make_tuple(n_mblocks, Hq, B, sms);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+  }
+  auto span = [&](int T) {
+    std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+    for (int i = 0; i < sms; ++i) free_at.push(0.0);
+    double end = 0.0;
+    auto put = [&](double cost) {
+      const double t = free_at.top() + cost;
+      free_at.pop();
+      free_at.push(t);
+      end = t > end ? t : end;
+    };
+    for (int b = 0; b < B; ++b) {
+      for (int mb = n_mblocks - 1; mb >= n_mblocks - T; --mb)
+        for (int h = 0; h < Hq; ++h) put(kFix + kSingle * (mb + 1));
+      for (int mb = n_mblocks - T - 1; mb >= 0; --mb)
+        for (int h = 0; h < Hq / 2; ++h) put(kFix + kPair * (mb + 1));
+    }
+    return end;
+  };
+  int best_t = 0;
+  double best = span(0);
+  for (int T = 1; T < n_mblocks && T <= 64; ++T) {
+    const double sp = span(T);
+    if (sp < best * 0.995) {
+      best = sp;
+      best_t = T;
+    }
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  memo[key] = best_t;
+  return best_t;
+}
 }  // namespace
 
 extern "C" {
@@ -339,8 +398,10 @@ int tg_keybias_attn_fwd(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   if ((st = device_error_ptr(&p.err))) return st;
 
+  p.n_single_rows = (p.pair_heads && p.causal) ? attn_single_rows(p.n_mblocks, Hq, B, sm_count()) : 0;
   const int64_t units =
-      p.pair_heads ? (int64_t)p.n_mblocks * (Hq / 2) : (int64_t)((p.n_mblocks + 1) / 2) * Hq;
+      p.pair_heads ? (int64_t)(p.n_mblocks - p.n_single_rows) * (Hq / 2) + (int64_t)p.n_single_rows * Hq
+                   : (int64_t)((p.n_mblocks + 1) / 2) * Hq;
   if (units > 0x7fffffff) return fail(TG_ERR_UNSUPPORTED, "problem too large");
 
   int dev;

@@ -83,16 +83,17 @@ class _L2Flush:
 
 def _time_flushed(fn, flush, iters=10, warmup=3):
     """Median CUDA-event ms of one fn() launch, L2 flushed before each. A
-    ~100 us device spin after the flush keeps the GPU busy while the host
-    issues the start event and the launch, so the events bracket the
-    kernel's own time and not the host's launch path."""
+    ~1 ms device spin after the flush keeps the GPU busy while the host
+    issues the start event and the launch (the Python op path takes tens of
+    microseconds), so the events bracket the kernel's own time and not the
+    host's launch path."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     ts = []
     for _ in range(iters):
         flush()
-        torch.cuda._sleep(200_000)
+        torch.cuda._sleep(2_000_000)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()
