@@ -282,6 +282,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched with programmatic stream serialization: the prologue above
+  // (barriers, TMEM) overlaps the previous kernel's drain, and nothing that
+  // kernel may write (x, the rotary rows, the gains) is read or written
+  // before this wait. A CTA of this kernel and one of the attention kernel
+  // cannot share an SM (shared memory), so TMEM is never contended.
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == kGsProducerWarp) {
     // ------------------------------------------------------------ producer

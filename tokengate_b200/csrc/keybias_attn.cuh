@@ -326,6 +326,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched with programmatic stream serialization: the prologue above
+  // (barriers, the Q extension, TMEM) overlaps the previous kernel's drain;
+  // Q/K/V, the bias and the row scale are read only after this wait.
+  griddep_wait();
+  griddep_launch_dependents();
 
   // Register split (launch: 384 threads x 168 = 64512): the two softmax
   // warpgroups take 192 each, the producer/MMA warpgroup keeps 120:

@@ -176,7 +176,8 @@ int encode_2d_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t col
 
 namespace {
 // Launch with programmatic stream serialization, for the kernels of the
-// layer chains (layer glue, decode attention, gemv): the kernel may start
+// layer chains (layer glue, projections, attention, decode attention, gemv):
+// the kernel may start
 // while the previous kernel on the stream drains, and waits on the device
 // (griddep_wait) before it touches anything that kernel writes. Under a
 // stream capture this becomes a programmatic edge of the graph.
@@ -255,9 +256,9 @@ int launch_gemm_pair(const void* x, int64_t ld_x, const void* w, int64_t w_rows,
   cudaError_t e = smem_limit_once(tg::gemm_pair_kernel<kEpi>, tg::GemmLayout<kEpi>::kSmemBytes, attr_set, dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_pair smem)");
   const int64_t clusters = std::max<int64_t>(1, std::min<int64_t>(n_tiles, sm_count() / 2));
-  tg::gemm_pair_kernel<kEpi><<<(unsigned)(2 * clusters), tg::kGsThreads, tg::GemmLayout<kEpi>::kSmemBytes,
-                              static_cast<cudaStream_t>(stream)>>>(tx, tw, p);
-  e = cudaGetLastError();
+  e = launch_pdl(tg::gemm_pair_kernel<kEpi>, dim3((unsigned)(2 * clusters)), dim3(tg::kGsThreads),
+                 (size_t)tg::GemmLayout<kEpi>::kSmemBytes, static_cast<cudaStream_t>(stream), tx, tw, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, name);
   return TG_OK;
 }
@@ -420,13 +421,12 @@ int tg_keybias_attn_fwd(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
     }
   }
   dim3 grid((unsigned)units, (unsigned)B);
-  if (p.bias != nullptr)
-    tg::keybias_attn_fwd_kernel<true><<<grid, tg::kAttnThreads, tg::kAttnSmemBytes,
-                                        static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-  else
-    tg::keybias_attn_fwd_kernel<false><<<grid, tg::kAttnThreads, tg::kAttnSmemBytes,
-                                         static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = p.bias != nullptr
+      ? launch_pdl(tg::keybias_attn_fwd_kernel<true>, grid, dim3(tg::kAttnThreads), (size_t)tg::kAttnSmemBytes,
+                   static_cast<cudaStream_t>(stream), tq, tk, tv, p)
+      : launch_pdl(tg::keybias_attn_fwd_kernel<false>, grid, dim3(tg::kAttnThreads), (size_t)tg::kAttnSmemBytes,
+                   static_cast<cudaStream_t>(stream), tq, tk, tv, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "keybias attention launch");
   return TG_OK;
 }
