@@ -278,6 +278,30 @@ int tg_branch_score(const void* gu, int64_t gu_sb, int64_t gu_ss, int inter, con
                     int64_t s_sb, void* stream);
 
 /*
+ * a4 (finalized gate), fused — the scoring branch from the LN2-normalised
+ * rows themselves: the [gate | up] projection GEMM with the SwiGLU and the
+ * readout row in its epilogue, so the projection never reaches memory:
+ *   score[m] = bf16( sum_c bf16(bf16(silu(G[m, c])) * U[m, c]) * w_readout[c] )
+ *   G = bf16(x W_gate^T), U = bf16(x W_up^T), silu with IEEE operations only
+ * (the activations of tg_branch_score, on this GEMM's own projection). The
+ * epilogue leaves one fp32 partial dot per row and 64-column half tile in
+ * `partial`; a second kernel on the same stream adds a row's partials in
+ * index order and rounds to bf16 (-0 stored as +0). The projection's and the
+ * dot's fp32 summation orders are this kernel's own: against the GEMM +
+ * tg_branch_score chain a score can differ in its last bf16 bits.
+ * Same operation as the reference's gate_branch_hs -> br(z)
+ * (tokengate/e2e_gate/gate_module/gate_forward.py:491-524, :330-340).
+ *
+ * x: bf16 (M, K) row stride ld_x (the state rows of one request);
+ * w_gu: bf16 (2*inter, K) = [W_gate; W_up] row stride ld_w; w_readout: bf16
+ * (inter,), 16-byte aligned; partial: caller workspace of (inter/64) * M
+ * floats; scores: fp32 (M,). K a multiple of 64, inter a multiple of 128.
+ * M == 0 returns TG_OK without touching the pointers.
+ */
+int tg_gemm_swiglu_readout(const void* x, int64_t ld_x, const void* w_gu, int64_t ld_w, const void* w_readout,
+                           float* partial, float* scores, int64_t M, int K, int inter, void* stream);
+
+/*
  * The finalized gate's Phase-2 operands of every biased layer
  * from the raw branch scores, in one launch. For request b, kept slot t
  * (position p = keep[b, t]), Phase-2 layer l and head h:

@@ -215,11 +215,24 @@ def _logit_check(got, ref, max_abs=0.15, min_cos=0.999):
     assert err <= max_abs and cos >= min_cos, f"logits max-abs {err} cos {cos}"
 
 
-def test_e2e_prefill_vs_reference_fixture_and_stages(tiny_e2e, monkeypatch):
+@pytest.mark.parametrize("fused", [False, True])
+def test_e2e_prefill_vs_reference_fixture_and_stages(tiny_e2e, monkeypatch, fused):
+    """fused=False: the [gate | up] GEMM + branch_score readout, whose scores
+    are checked bit for bit against the oracle on the GPU's own projection;
+    fused=True: the branch as one GEMM with the readout in its epilogue (no
+    projection to check against), scores within a bf16 ulp of the unfused
+    chain's. Both: the selection on the kernel's scores, tables, and result
+    parity with the reference's own run."""
     d, model, gate = tiny_e2e["d"], tiny_e2e["model"], tiny_e2e["gate"]
     prompts = [d["prompt0"].tolist(), d["prompt1"].tolist()]
     starts, ends, K = d["starts"].tolist(), d["ends"].tolist(), int(d["K"])
+    monkeypatch.setattr(tgp, "_BRANCH_FUSED", False)
     seen = _record(monkeypatch)
+    if fused:
+        tgp.prefill_batch_for_decode(model, gate, prompts, starts, ends, 1, K)
+        unfused_scores = [seen["sel_scores"][b, :ends[b] - starts[b]].clone() for b in range(2)]
+        monkeypatch.setattr(tgp, "_BRANCH_FUSED", True)
+        seen.clear()
     logits = []
     h = model.lm_head.register_forward_hook(lambda m, a, o: logits.append(o.detach()))
     try:
@@ -234,10 +247,19 @@ def test_e2e_prefill_vs_reference_fixture_and_stages(tiny_e2e, monkeypatch):
     # selection on the aggregate of those scores (bit-exact), the tables (bf16 values)
     raws = []
     for b in range(2):
-        gu = seen["gu"][b][0]
-        ref = ge.branch_score(_bits(gu), _bits(seen["w_row"]))
         got = seen["sel_scores"][b, :ends[b] - starts[b]].cpu().numpy()
-        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        if fused:
+            assert "gu" not in seen
+            ref = got
+            un = unfused_scores[b].cpu().numpy()
+            # the GEMM's and the dot's own fp32 orders: about a bf16 ulp of the score
+            # (or of the row's scale, under cancellation); most scores equal
+            assert (np.abs(got - un) <= 2.0 ** -7 * np.abs(un) + 2.0 ** -9 * np.abs(un).max()).all()
+            assert (got == un).mean() >= 0.8, f"{(got == un).mean():.3f} of the scores equal"
+        else:
+            gu = seen["gu"][b][0]
+            ref = ge.branch_score(_bits(gu), _bits(seen["w_row"]))
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
         raws.append(ref)
         agg = ge.aggregate(ge.e2e_bias(ref, seen["gs"].cpu().numpy()))
         top = ge.select(agg, K_cl[b])

@@ -89,6 +89,7 @@ _SIGNATURES = {
     "tg_gemm_qkv_rope": [_P, _I64, _P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _I64,
                          _I32, _F, _P],
     "tg_branch_score": [_P, _I64, _I64, _I32, _P, _I32, _P, _P, _P, _I64, _P],
+    "tg_gemm_swiglu_readout": [_P, _I64, _P, _I64, _P, _P, _P, _I64, _I32, _I32, _P],
     "tg_phase2_tables": [_P, _I64, _I32, _P, _P, _P, _I64, _P, _I32, _P, _P, _I32, _I32, _F, _F, _P, _P,
                          _P],
     "tg_decode_attn": [_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64,

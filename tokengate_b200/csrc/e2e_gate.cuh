@@ -22,6 +22,12 @@
 //   shared memory), which takes the SiLU's ~30 instructions per element off
 //   the issue path of an otherwise HBM-bound pass.
 //
+// branch_reduce_kernel — the fused form of the same readout: the branch GEMM
+//   (gemm_pair.cuh, EPI_SWIGLU_READOUT) leaves one fp32 partial dot per row
+//   and 64-column half tile; this kernel adds a row's partials in index order
+//   and rounds to bf16. Same activations and rounding points, another fp32
+//   summation order (and the GEMM's own [gate | up] accumulation order).
+//
 // phase2_tables_kernel — everything between the raw score and the attention
 //   kernel's operands, for all Phase-2 layers in one launch:
 //     rs    = rsqrt(mean_state(x^2) + eps)           E2EGate._seq_rms_norm_qwen
@@ -194,6 +200,29 @@ __global__ void __launch_bounds__(kBranchThreads, 1) branch_score_kernel(const B
       p.out[(int64_t)req * p.out_sb + r] = s == 0.0f ? 0.0f : s;
     }
   }
+}
+
+// Readout of the fused branch GEMM (gemm_pair EPI_SWIGLU_READOUT): score[r]
+// = bf16(sum of partial[i][r] over i = 0..n_part-1 in index order), stored as
+// fp32 with -0 replaced by +0. One thread per row; launched with programmatic
+// stream serialization right after the GEMM that writes the partials.
+struct BranchReduceParams {
+  const float* partial;  // (n_part, ld_partial)
+  int64_t ld_partial;
+  int n_part;
+  int64_t M;
+  float* out;            // (M,)
+};
+
+__global__ void __launch_bounds__(256) branch_reduce_kernel(const BranchReduceParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (r >= p.M) return;
+  float acc = 0.f;
+  for (int i = 0; i < p.n_part; ++i) acc = __fadd_rn(acc, p.partial[(int64_t)i * p.ld_partial + r]);
+  const float s = bf16_round(acc);
+  p.out[r] = s == 0.0f ? 0.0f : s;
 }
 
 struct TablesParams {

@@ -5,6 +5,13 @@
 //      out[m, c] = bf16( bf16(silu(G[m, c])) * U[m, c] ),  c < inter,
 //      G = bf16(x W_gate^T), U = bf16(x W_up^T), W = the fused [W_gate; W_up]
 //    = modeling_qwen3.Qwen3MLP's act_fn(gate_proj(x)) * up_proj(x) in bf16;
+//  * EPI_SWIGLU_READOUT, the finalized gate's scoring branch (the same
+//    SwiGLU of its [W_gate; W_up] projection, silu by the IEEE-only tg_silu
+//    as the branch readout computes it) folded into its one-row readout:
+//      partial[2 nt + h][m] = sum over the tile's 64 columns c of half h of
+//                             bf16(bf16(silu(G[m, c])) * U[m, c]) * w[c]
+//    (fp32, fused multiply-adds in column order); branch_reduce_kernel adds
+//    a row's partials in index order and rounds the score to bf16;
 //  * EPI_QKV_ROPE, the attention input projection:
 //      out[m, :] = [q heads | k heads | v heads] of bf16(x W_qkv^T), W = the
 //      fused [W_q; W_k; W_v], with every q and k head RMS-normalised by its
@@ -43,6 +50,7 @@
 #pragma once
 
 #include "layer_glue.cuh"
+#include "e2e_gate.cuh"
 
 namespace tg {
 
@@ -55,7 +63,7 @@ constexpr int kGsStageBytes = 2 * kGsTileBytes;
 
 constexpr unsigned int ERR_GEMM = 1u << 14;
 
-enum GemmEpilogue { EPI_SWIGLU = 0, EPI_QKV_ROPE = 1 };
+enum GemmEpilogue { EPI_SWIGLU = 0, EPI_QKV_ROPE = 1, EPI_SWIGLU_READOUT = 2 };
 
 // Shared-memory layout per epilogue. The q/k/v epilogue stages each tile's
 // 128 rotary cos / sin rows (256 B each, rows padded to 272 B so that the
@@ -104,6 +112,10 @@ struct GemmPairParams {
   int64_t cs_sb, cs_ss;
   int seq;
   float eps;
+  // EPI_SWIGLU_READOUT
+  const __nv_bfloat16* w_readout;  // (inter,) readout row
+  float* partial;                  // (2 * n_tiles_n, ld_partial) per-half partial dots
+  int64_t ld_partial;
   unsigned int* err;
 };
 
@@ -415,7 +427,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
         if (lane == 0) mbar_arrive(bar(Lay::kCsFull));
         if (!warp_wait(bar(Lay::kCsFull), (uint32_t)n_staged & 1u, p.err, ERR_GEMM)) break;
       }
-      if constexpr (kEpi == EPI_SWIGLU) {
+      if constexpr (kEpi == EPI_SWIGLU_READOUT) {
+        // this row's 64 SwiGLU activations of the tile's half, dotted with
+        // the readout row in column order
+        const int col0 = nt * 128 + half * 64;
+        const uint32_t tacc = tmem + lane_off + (uint32_t)buf * 256u + (uint32_t)half * 64u;
+        float dot = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tacc + c * 32, g);
+          tmem_ld32(tacc + 128 + c * 32, u);
+          const uint4* wv = reinterpret_cast<const uint4*>(p.w_readout + col0 + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 w4 = __ldg(wv + q);
+            const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int k = q * 8 + e;
+              const float gb = round_bf16(__uint_as_float(g[k]));
+              const float ub = round_bf16(__uint_as_float(u[k]));
+              const float a = round_bf16(__fmul_rn(round_bf16(tg_silu(gb)), ub));
+              const float wk = (e & 1) ? bf16_hi(ww[e >> 1]) : bf16_lo(ww[e >> 1]);
+              dot = __fmaf_rn(a, wk, dot);
+            }
+          }
+        }
+        if (lane < nvalid) p.partial[(int64_t)(2 * nt + half) * p.ld_partial + row0 + lane] = dot;
+      } else if constexpr (kEpi == EPI_SWIGLU) {
         const int col0 = nt * 128 + half * 64;
         const uint32_t tacc = tmem + lane_off + (uint32_t)buf * 256u + (uint32_t)half * 64u;
 #pragma unroll 1

@@ -811,6 +811,47 @@ int tg_gemm_swiglu(const void* x, int64_t ld_x, const void* w_gu, int64_t ld_w, 
   return launch_gemm_pair<tg::EPI_SWIGLU>(x, ld_x, w_gu, 2 * (int64_t)inter, ld_w, p, stream, "gemm_swiglu");
 }
 
+int tg_gemm_swiglu_readout(const void* x, int64_t ld_x, const void* w_gu, int64_t ld_w, const void* w_readout,
+                           float* partial, float* scores, int64_t M, int K, int inter, void* stream) {
+  if (M < 0 || K < 1 || inter < 1)
+    return fail(TG_ERR_INVALID_ARGUMENT, "gemm_swiglu_readout: M=%lld K=%d inter=%d", (long long)M, K, inter);
+  if (M == 0) return TG_OK;
+  if (x == nullptr || w_gu == nullptr || w_readout == nullptr || partial == nullptr || scores == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "gemm_swiglu_readout: NULL argument");
+  if (K % tg::kGsBK != 0)
+    return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu_readout: K=%d must be a multiple of %d", K, tg::kGsBK);
+  if (inter % 128 != 0)
+    return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu_readout: inter=%d must be a multiple of 128", inter);
+  if (M > (int64_t)INT32_MAX - 256)
+    return fail(TG_ERR_UNSUPPORTED, "gemm_swiglu_readout: M=%lld too large", (long long)M);
+  if (reinterpret_cast<uintptr_t>(w_readout) & 15)
+    return fail(TG_ERR_ALIGNMENT, "gemm_swiglu_readout: w_readout must be 16-byte aligned");
+  tg::GemmPairParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = (int)M;
+  p.K = K;
+  p.n_tiles_n = inter / 128;
+  p.b_step = 128;  // as gemm_swiglu: rank 0 the W_gate rows, rank 1 the matching W_up rows
+  p.b_rank1 = inter;
+  p.w_readout = static_cast<const __nv_bfloat16*>(w_readout);
+  p.partial = partial;
+  p.ld_partial = M;
+  int st = launch_gemm_pair<tg::EPI_SWIGLU_READOUT>(x, ld_x, w_gu, 2 * (int64_t)inter, ld_w, p, stream,
+                                                    "gemm_swiglu_readout");
+  if (st) return st;
+  tg::BranchReduceParams r;
+  r.partial = partial;
+  r.ld_partial = M;
+  r.n_part = inter / 64;
+  r.M = M;
+  r.out = scores;
+  cudaError_t e = launch_pdl(tg::branch_reduce_kernel, dim3((unsigned)((M + 255) / 256)), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), r);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "branch_reduce launch");
+  return TG_OK;
+}
+
 int tg_gemm_qkv_rope(const void* x, int64_t ld_x, const void* w_qkv, int64_t ld_w, void* out, int64_t ld_out,
                      int64_t M, int K, int n_q_heads, int n_k_heads, const void* q_norm_w, const void* k_norm_w,
                      const void* cos, const void* sin, int64_t cs_sb, int64_t cs_ss, int seq, float eps,

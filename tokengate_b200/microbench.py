@@ -120,7 +120,9 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
     `hbm_peak_gbs`. branch_score: the finalized gate's readout over the same
     state rows' bf16 [gate | up] projections (inter 6144), GB/s of those rows
     + the readout row + fp32 scores (the SiLU table build included in the
-    time). gemm_swiglu: the MLP up-projection with the SwiGLU
+    time). branch_fused: the whole branch of one request's 32000 state rows
+    as one GEMM with the SwiGLU and readout epilogue, TFLOP/s of
+    2*M*2048*12288, beside cuBLAS's [gate | up] GEMM + branch_score. gemm_swiglu: the MLP up-projection with the SwiGLU
     epilogue at hidden 2048, intermediate 6144 and M = 2768 (Phase 2) and
     32768 (Phase 1) rows: TFLOP/s of 2*M*2048*12288, beside cuBLAS's bf16
     GEMM into [gate | up] alone and with the silu_mul kernel after it (the
@@ -130,8 +132,8 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
     g = torch.Generator(device=dev).manual_seed(0)
     flush = _L2Flush(dev)
     out = {"timing": f"CUDA events, median of {iters} launches, L2 flushed (a 256 MB read) before each",
-           "attention": [], "gate_score": [], "topk": [], "gather": [], "branch_score": [], "gemm_swiglu": [],
-           "gemm_qkv_rope": []}
+           "attention": [], "gate_score": [], "topk": [], "gather": [], "branch_score": [], "branch_fused": [],
+           "gemm_swiglu": [], "gemm_qkv_rope": []}
     for S, kind in ((4096, "per-key bias"), (2768, "Phase-2 bias row"), (8192, "no bias"), (32768, "no bias")):
         q = torch.randn(1, S, 16, 128, device=dev, dtype=torch.bfloat16, generator=g)
         k = torch.randn(1, S, 8, 128, device=dev, dtype=torch.bfloat16, generator=g)
@@ -188,6 +190,18 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
         del gu, bs
     K, inter = 2048, 6144
     w = (torch.randn(2 * inter, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+    x = (torch.randn(n_art, K, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    wr = (torch.randn(inter, device=dev, generator=g) * inter ** -0.5).to(torch.bfloat16)
+    sc = torch.empty(n_art, device=dev)
+    ms = _time_flushed(lambda: ops.gemm_swiglu_readout(x, w, wr, out=sc), flush, iters)
+    gu = torch.nn.functional.linear(x, w)
+    ms_lin = _time_flushed(lambda: torch.nn.functional.linear(x, w), flush, iters)
+    ms_rd = _time_flushed(lambda: ops.branch_score(gu.unsqueeze(0), wr, [0], [n_art]), flush, iters)
+    flops = 2.0 * n_art * K * 2 * inter
+    out["branch_fused"].append(dict(rows=n_art, K=K, inter=inter, us=ms * 1e3, tflops=flops / ms / 1e9,
+                                    frac=flops / ms / 1e9 / tflops_peak, cublas_gemm_us=ms_lin * 1e3,
+                                    cublas_plus_branch_score_us=(ms_lin + ms_rd) * 1e3))
+    del x, gu
     for M in (2768, 32768):
         x = (torch.randn(M, K, device=dev, generator=g) * 0.5).to(torch.bfloat16)
         flops = 2.0 * M * K * 2 * inter

@@ -435,6 +435,39 @@ def gemm_swiglu(x: torch.Tensor, w_gu: torch.Tensor, inter: int) -> torch.Tensor
     return out
 
 
+def gemm_swiglu_readout(x: torch.Tensor, w_gu: torch.Tensor, w_readout: torch.Tensor,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The finalized gate's scoring branch fused into one tcgen05 GEMM: x (M, K) rows, w_gu
+    (2*inter, K) = [W_gate; W_up], w_readout (inter,) -> fp32 scores (M,) =
+    bf16(sum_c bf16(bf16(silu(G[:, c])) * U[:, c]) * w_readout[c]) with [G | U] the bf16 projection,
+    silu with IEEE operations only. The [gate | up] projection never reaches memory; the partial
+    dots go through an (inter/64, M) fp32 workspace allocated here."""
+    _require_cuda("x", x, torch.bfloat16)
+    _require_cuda("w_gu", w_gu, torch.bfloat16)
+    _require_cuda("w_readout", w_readout, torch.bfloat16)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be (M, K) with a contiguous last dim")
+    M, K = x.shape
+    if w_readout.dim() != 1 or not w_readout.is_contiguous():
+        raise ValueError("w_readout must be a contiguous vector")
+    inter = w_readout.shape[0]
+    if w_gu.dim() != 2 or w_gu.stride(1) != 1 or w_gu.shape != (2 * inter, K):
+        raise ValueError(f"w_gu must be (2*inter, K) = ({2 * inter}, {K}) with a contiguous last dim")
+    if out is None:
+        out = torch.empty(M, dtype=torch.float32, device=x.device)
+    else:
+        _require_cuda("out", out, torch.float32)
+        if out.dim() != 1 or out.shape[0] < M or out.stride(0) != 1:
+            raise ValueError("out must be a contiguous fp32 vector of >= M entries")
+    part = torch.empty((max(inter // 64, 1), max(M, 1)), dtype=torch.float32, device=x.device)
+    L = _lib.lib()
+    with _device_ctx(x):
+        _lib.check_launch(L.tg_gemm_swiglu_readout(x.data_ptr(), x.stride(0), w_gu.data_ptr(), w_gu.stride(0),
+                                                   w_readout.data_ptr(), part.data_ptr(), out.data_ptr(), M, K,
+                                                   inter, _stream(x)))
+    return out
+
+
 def gemm_qkv_rope(x: torch.Tensor, w_qkv: torch.Tensor, n_q: int, n_k: int, q_norm_w: torch.Tensor,
                   k_norm_w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, eps: float) -> torch.Tensor:
     """x (B, S, K), w_qkv ((n_q + 2*n_k)*128, K) = [W_q; W_k; W_v] -> (B, S, n_q + 2*n_k, 128): the

@@ -67,17 +67,34 @@ def set_phase2_graphs(enabled: bool) -> None:
 # rows per scoring-branch GEMM: bounds the [gate | up] workspace (rows x 2*inter bf16)
 _BRANCH_CHUNK = 32768
 
+# The finalized gate's branch as one fused GEMM (ops.gemm_swiglu_readout: the
+# SwiGLU and the readout row in the projection's epilogue) where its shapes
+# allow; False runs the projection GEMM and the branch_score readout, whose
+# scores are reproducible bit for bit from that projection.
+_BRANCH_FUSED = True
+
+
+def set_branch_fused(enabled: bool) -> None:
+    global _BRANCH_FUSED
+    _BRANCH_FUSED = bool(enabled)
+
 
 def _branch_scores(ew, x2: torch.Tensor, starts: Sequence[int], n_state: Sequence[int]) -> torch.Tensor:
     """Raw scores of the finalized gate's branch over each request's state rows.
 
     x2: (B, S, H) bf16 = post_attention_layernorm(a_j) of the gate layer. Each
-    request's state rows are contiguous, so the fused [gate | up] GEMM runs on
-    them directly (no gather), in chunks of _BRANCH_CHUNK rows, followed by the
+    request's state rows are contiguous, so the branch runs on them directly
+    (no gather): the fused GEMM (SwiGLU + readout epilogue) per request, or
+    the [gate | up] GEMM in chunks of _BRANCH_CHUNK rows followed by the
     branch_score readout. Returns fp32 (B, max n_state)."""
     B = x2.shape[0]
     scores = torch.empty((B, max(n_state)), dtype=torch.float32, device=x2.device)
+    inter = ew.w_row.shape[0]
+    fused = _BRANCH_FUSED and inter % 128 == 0 and x2.shape[-1] % 64 == 0
     for b in range(B):
+        if fused:
+            ops.gemm_swiglu_readout(x2[b, starts[b]:starts[b] + n_state[b]], ew.wgu, ew.w_row, out=scores[b])
+            continue
         for c0 in range(0, n_state[b], _BRANCH_CHUNK):
             c1 = min(n_state[b], c0 + _BRANCH_CHUNK)
             gu = torch.nn.functional.linear(x2[b, starts[b] + c0:starts[b] + c1], ew.wgu)
