@@ -42,6 +42,14 @@ int tg_abi_version(void);
 /* Message of the calling thread's last failed call ("" if none). */
 const char* tg_last_error(void);
 
+/* Host-side scan of a prompt's ids for the state-span sentinels
+ * (split_state_span, tokengate/e2e_gate/gate_module/gate_forward.py:664-689):
+ * counts of start_id / end_id in ids[0, n) and the first position of each
+ * (-1 when absent). A valid span has exactly one of each, start first. No
+ * device work; ids is host memory. */
+int tg_find_state_span(const int64_t* ids, int64_t n, int64_t start_id, int64_t end_id, int64_t* first_start,
+                       int64_t* first_end, int64_t* n_start, int64_t* n_end);
+
 /* Reads the device-side error word of the current device (bit flags set by a
  * kernel whose bounded wait timed out; 0 = none). Synchronises `stream`.
  * clear != 0 resets the word to 0 afterwards. */

@@ -114,6 +114,26 @@ def test_state_span():
             split_state_span(bad)
 
 
+def test_find_state_span_matches_numpy():
+    """The library's host scan: counts and first positions of both sentinels,
+    against numpy, on random ids with 0, 1 or 2 of each (and empty input)."""
+    L = _lib.lib()
+    rng = np.random.default_rng(3)
+    for n in (0, 1, 7, 1000, 32768):
+        for _ in range(6):
+            a = rng.integers(0, 151000, n).astype(np.int64)
+            for sid in (STATE_START_ID, STATE_END_ID):
+                for pos in rng.integers(0, max(n, 1), rng.integers(0, 3)) if n else ():
+                    a[pos] = sid
+            out = [ctypes.c_int64() for _ in range(4)]
+            assert L.tg_find_state_span(a.ctypes.data, a.size, STATE_START_ID, STATE_END_ID,
+                                        *[ctypes.byref(o) for o in out]) == 0
+            fs, fe, ns, ne = (o.value for o in out)
+            ss, ee = np.flatnonzero(a == STATE_START_ID), np.flatnonzero(a == STATE_END_ID)
+            assert (ns, ne) == (len(ss), len(ee))
+            assert fs == (ss[0] if len(ss) else -1) and fe == (ee[0] if len(ee) else -1)
+
+
 def test_state_span_tensor_inputs():
     """The generate path's splitter takes a list, an int64 / int32 CPU tensor
     or a numpy array; on CPU (no CUDA device given) every form gives the

@@ -63,6 +63,7 @@ _F = ctypes.c_float
 # name -> argtypes, in header order
 _SIGNATURES = {
     "tg_abi_version": [],
+    "tg_find_state_span": [_P, _I64, _I64, _I64, _P, _P, _P, _P],
     "tg_last_error": [],
     "tg_device_error": [_P, ctypes.POINTER(ctypes.c_uint), _I32],
     "tg_keybias_attn_fwd": [

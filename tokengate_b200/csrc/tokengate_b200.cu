@@ -324,6 +324,30 @@ int tg_abi_version(void) { return TG_ABI_VERSION; }
 
 const char* tg_last_error(void) { return g_last_error; }
 
+int tg_find_state_span(const int64_t* ids, int64_t n, int64_t start_id, int64_t end_id, int64_t* first_start,
+                       int64_t* first_end, int64_t* n_start, int64_t* n_end) {
+  if (n < 0 || (n > 0 && ids == nullptr) || first_start == nullptr || first_end == nullptr || n_start == nullptr ||
+      n_end == nullptr)
+    return fail(TG_ERR_INVALID_ARGUMENT, "find_state_span: NULL argument or n=%lld", (long long)n);
+  // one pass: counts of both sentinels (branch-free, vectorisable), then the
+  // first position of each, searched only when it occurs
+  int64_t cs = 0, ce = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    cs += ids[i] == start_id;
+    ce += ids[i] == end_id;
+  }
+  int64_t fs = -1, fe = -1;
+  for (int64_t i = 0; cs > 0 && i < n; ++i)
+    if (ids[i] == start_id) { fs = i; break; }
+  for (int64_t i = 0; ce > 0 && i < n; ++i)
+    if (ids[i] == end_id) { fe = i; break; }
+  *first_start = fs;
+  *first_end = fe;
+  *n_start = cs;
+  *n_end = ce;
+  return TG_OK;
+}
+
 int tg_device_error(void* stream, unsigned int* flags_out, int clear) {
   if (flags_out == nullptr) return fail(TG_ERR_INVALID_ARGUMENT, "flags_out is NULL");
   unsigned int* dptr;

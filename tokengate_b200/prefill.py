@@ -33,6 +33,7 @@ host-side index construction are replaced by three batched launches; no host
 synchronisation happens between Phase 1 and the head.
 """
 import array
+import weakref
 from typing import List, Optional, Sequence, Union
 
 import torch
@@ -100,6 +101,27 @@ def _branch_scores(ew, x2: torch.Tensor, starts: Sequence[int], n_state: Sequenc
             gu = torch.nn.functional.linear(x2[b, starts[b] + c0:starts[b] + c1], ew.wgu)
             ops.branch_score(gu.unsqueeze(0), ew.w_row, [0], [c1 - c0], out=scores[b:b + 1, c0:])
     return scores
+
+
+# Phase 1's rotary tables: cos / sin of positions 0..S-1 depend only on the
+# rotary module and S, so the fused path computes them once per (module, S,
+# device, dtype) and reuses them (expanded over the batch) on later prefills.
+_PHASE1_ROPE: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+_PHASE1_ROPE_MAX = 4
+
+
+def _phase1_rope(rotary_emb, hidden: torch.Tensor, S: int, B: int):
+    key = (S, hidden.device, hidden.dtype)
+    per_mod = _PHASE1_ROPE.setdefault(rotary_emb, {})
+    hit = per_mod.get(key)
+    if hit is None:
+        pos = torch.arange(S, device=hidden.device).unsqueeze(0)
+        cos, sin = rotary_emb(hidden[:1, :S], pos)
+        if len(per_mod) >= _PHASE1_ROPE_MAX:
+            per_mod.pop(next(iter(per_mod)))
+        hit = per_mod[key] = (cos.contiguous(), sin.contiguous())
+    cos, sin = hit
+    return cos.expand(B, -1, -1), sin.expand(B, -1, -1)
 
 
 def _ids_to_device(prompt_ids_list, device) -> torch.Tensor:
@@ -183,12 +205,11 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
     ids = _ids_to_device(prompt_ids_list, device)
     set_gate_bias_for_layers(model, 0, gate_layer + 1, None)
     hidden = inner.embed_tokens(ids)
-    position_ids = torch.arange(max_seq_len, device=device).unsqueeze(0).expand(B, -1)
-    pe = inner.rotary_emb(hidden, position_ids)
     cache = PrefillCache(n_layers)
     x2 = None
+    pe = None
     if fused:
-        cos, sin = pe
+        cos, sin = _phase1_rope(inner.rotary_emb, hidden, max_seq_len, B)
         delta = None
         for i in range(gate_layer if e2e else gate_layer + 1):
             hidden, delta = layer_forward(fw[i], hidden, delta, cos, sin, cache, i)
@@ -198,6 +219,8 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
             hidden, _ = ops.add_rmsnorm(hidden, delta, None, 0.0, h_out=hidden, want_x=False)
         del delta, cos, sin
     else:
+        position_ids = torch.arange(max_seq_len, device=device).unsqueeze(0).expand(B, -1)
+        pe = inner.rotary_emb(hidden, position_ids)
         for i in range(gate_layer + 1):
             hidden = inner.layers[i](hidden, attention_mask=None, position_ids=position_ids,
                                      past_key_values=cache, use_cache=True, position_embeddings=pe)
