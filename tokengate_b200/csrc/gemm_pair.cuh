@@ -101,8 +101,12 @@ struct GemmPairParams {
   int n_tiles_n;   // column tiles
   int n_tiles_m;   // ceil(M / 256)
   int n_tiles;     // n_tiles_m * n_tiles_n
+  int n_wide;      // tiles [0, n_wide) run whole (N = 256) in rounds over the clusters
+  int n_narrow;    // items after them: half j = i & 1 (N = 128) of tile n_wide + i / 2, i < n_narrow
   int b_step;      // weight rows per column tile for rank 0 (SwiGLU 128, q/k/v 256)
   int b_rank1;     // rank 1's weight rows, offset from rank 0's (SwiGLU inter, q/k/v 128)
+  int nb_step;     // narrow half j: rank 0's weight rows start at nt * b_step + j * nb_step
+  int nb_rank1;    //   and rank 1's nb_rank1 after them (SwiGLU 64 / inter, q/k/v 128 / 64)
   // EPI_QKV_ROPE
   int n_q, n_k, n_heads;          // q heads, k heads, all heads (q + k + v)
   const __nv_bfloat16* q_w;       // (128,) q_norm gains
@@ -247,10 +251,32 @@ __device__ __forceinline__ void qkv_rope_head(const GemmPairParams& p, uint32_t 
   }
 }
 
+// Work item k of cluster cid: its wide tiles cid, cid + n_clusters, ... below
+// n_wide, then, when cid < n_narrow, one narrow item: half j = cid & 1 of
+// tile n_wide + cid / 2. A launch whose last round would leave most CTA
+// pairs idle runs that round's tiles as twice as many half-width items, each
+// half the MMA time (j = -1 marks a wide tile). False past the last item.
+__device__ __forceinline__ bool gemm_item(const GemmPairParams& p, int cid, int n_clusters, int k, int& t,
+                                          int& j) {
+  const int n_mine = cid < p.n_wide ? (p.n_wide - cid + n_clusters - 1) / n_clusters : 0;
+  if (k < n_mine) {
+    t = cid + k * n_clusters;
+    j = -1;
+    return true;
+  }
+  if (k == n_mine && cid < p.n_narrow) {
+    t = p.n_wide + (cid >> 1);
+    j = cid & 1;
+    return true;
+  }
+  return false;
+}
+
 template <int kEpi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
-                     const __grid_constant__ CUtensorMap tm_w, const GemmPairParams p) {
+                     const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_w64, const GemmPairParams p) {
   using Lay = GemmLayout<kEpi>;
   constexpr int kStages = Lay::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -307,19 +333,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
       tma_prefetch_desc(&tm_w);
+      if (p.n_narrow > 0) tma_prefetch_desc(&tm_w64);
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = cid; ok && t < p.n_tiles; t += n_clusters) {
+      int t, j;
+      for (int k = 0; ok && gemm_item(p, cid, n_clusters, k, t, j); ++k) {
         const int mt = t / p.n_tiles_n, nt = t - mt * p.n_tiles_n;
+        const bool narrow = j >= 0;
         const int a_row = mt * 256 + (int)rank * 128;
-        const int b_row = nt * p.b_step + (leader ? 0 : p.b_rank1);
+        const int b_row = narrow ? nt * p.b_step + j * p.nb_step + (leader ? 0 : p.nb_rank1)
+                                 : nt * p.b_step + (leader ? 0 : p.b_rank1);
+        // both CTAs' A rows and B rows (64 per CTA for a narrow item)
+        const uint32_t tx = narrow ? 2 * (kGsTileBytes + kGsTileBytes / 2) : 2 * kGsStageBytes;
+        const CUtensorMap* tmb = narrow ? &tm_w64 : &tm_w;
         for (int kb = 0; kb < n_kb; ++kb) {
           if (!mbar_wait(bar(Lay::kEmpty + s), ph ^ 1u, p.err, ERR_GEMM)) { ok = false; break; }
           const uint32_t dst = sbase + s * kGsStageBytes;
-          if (leader) mbar_arrive_expect_tx(bar(Lay::kFull + s), 2 * kGsStageBytes);
+          if (leader) mbar_arrive_expect_tx(bar(Lay::kFull + s), tx);
           tma_load_2d_pair(dst, &tm_x, lbar(Lay::kFull + s), kb * kGsBK, a_row);
-          tma_load_2d_pair(dst + kGsTileBytes, &tm_w, lbar(Lay::kFull + s), kb * kGsBK, b_row);
+          tma_load_2d_pair(dst + kGsTileBytes, tmb, lbar(Lay::kFull + s), kb * kGsBK, b_row);
           if (++s == kStages) { s = 0; ph ^= 1u; }
         }
       }
@@ -335,12 +368,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
     // ------------------------------------------------------------ MMA (rank 0)
     if (leader) {
       constexpr uint32_t kIdesc = umma_idesc_bf16(256, 256, 0, 0);
+      constexpr uint32_t kIdescNarrow = umma_idesc_bf16(256, 128, 0, 0);
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      int it = 0;
-      for (int t = cid; ok && t < p.n_tiles; t += n_clusters, ++it) {
+      int t, j;
+      for (int it = 0; ok && gemm_item(p, cid, n_clusters, it, t, j); ++it) {
         const int buf = it & 1;
+        const uint32_t idesc = j >= 0 ? kIdescNarrow : kIdesc;
         const uint32_t acc = tmem + (uint32_t)buf * 256u;
         // the epilogues of both CTAs have read this buffer's previous tile
         if (it >= 2 && !warp_wait(bar(Lay::kAccEmpty + buf), (uint32_t)((it >> 1) - 1) & 1u, p.err, ERR_GEMM)) {
@@ -359,7 +394,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < kGsBK / 16; ++kk)
               umma_ss_pair(acc, umma_desc_sw128(sa + kk * 32, 16, 1024), umma_desc_sw128(sb + kk * 32, 16, 1024),
-                           kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                           idesc, (kb > 0 || kk > 0) ? 1u : 0u);
             umma_commit_pair(lbar(Lay::kEmpty + s));
             umma_commit_pair(fbar(Lay::kEmpty + s));
           }
@@ -391,10 +426,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
         *reinterpret_cast<uint4*>(smem + Lay::kSmGain + lane * 16) = __ldg(reinterpret_cast<const uint4*>(src));
       }
     }
-    int it = 0, n_staged = 0;
-    for (int t = cid; t < p.n_tiles; t += n_clusters, ++it) {
+    int n_staged = 0;
+    int t, j;
+    for (int it = 0; gemm_item(p, cid, n_clusters, it, t, j); ++it) {
       const int buf = it & 1;
       const int mt = t / p.n_tiles_n, nt = t - mt * p.n_tiles_n;
+      // A wide tile: warp half h takes outputs 64h.. (SwiGLU; G in TMEM columns
+      // 64h.., U in 128 + 64h..) or head 2 nt + h (q/k/v, columns 128h..). A
+      // narrow item j holds 128 columns (G 0..63, U 64..127, or one head),
+      // which half 0 takes as a wide tile's half j would; half 1 only keeps
+      // the barrier protocol.
+      const bool narrow = j >= 0;
+      const int part = narrow ? j : half;               // the wide tile's half this warp computes
+      const bool active = !narrow || half == 0;
+      const uint32_t gcol = narrow ? 0u : (uint32_t)half * 64u;
+      const uint32_t ucol = narrow ? 64u : 128u + (uint32_t)half * 64u;
       const int64_t row0 = (int64_t)mt * 256 + (int)rank * 128 + sub * 32;  // the warp's first row
       const int64_t left = (int64_t)p.M - row0;
       const int nvalid = left <= 0 ? 0 : (left >= 32 ? 32 : (int)left);
@@ -402,14 +448,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
       // q/k tiles: stage this CTA's 128 rotary cos / sin rows (4096 16-byte
       // chunks, 16 per thread, coalesced along each row) while the
       // accumulator is still being computed
-      const bool rope = Lay::kRope && 2 * nt < p.n_q + p.n_k;
+      const bool rope = Lay::kRope && 2 * nt + (narrow ? j : 0) < p.n_q + p.n_k;
       if (rope) {
         if (n_staged > 0 &&
             !warp_wait(bar(Lay::kCsFree), (uint32_t)(n_staged - 1) & 1u, p.err, ERR_GEMM))
           break;
 #pragma unroll 4
-        for (int j = 0; j < 16; ++j) {
-          const int q = etid + 256 * j;           // 0..4095: cos chunks, then sin chunks
+        for (int jj = 0; jj < 16; ++jj) {
+          const int q = etid + 256 * jj;          // 0..4095: cos chunks, then sin chunks
           const int tab = q >> 11, rr = (q >> 4) & 127, ch = q & 15;
           int64_t grow = (int64_t)mt * 256 + (int)rank * 128 + rr;
           if (grow >= p.M) grow = p.M - 1;        // rows past M: any valid row
@@ -430,14 +476,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
       if constexpr (kEpi == EPI_SWIGLU_READOUT) {
         // this row's 64 SwiGLU activations of the tile's half, dotted with
         // the readout row in column order
-        const int col0 = nt * 128 + half * 64;
-        const uint32_t tacc = tmem + lane_off + (uint32_t)buf * 256u + (uint32_t)half * 64u;
+        const int col0 = nt * 128 + part * 64;
+        const uint32_t tacc = tmem + lane_off + (uint32_t)buf * 256u;
         float dot = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; active && c < 2; ++c) {
           uint32_t g[32], u[32];
-          tmem_ld32(tacc + c * 32, g);
-          tmem_ld32(tacc + 128 + c * 32, u);
+          tmem_ld32(tacc + gcol + c * 32, g);
+          tmem_ld32(tacc + ucol + c * 32, u);
           const uint4* wv = reinterpret_cast<const uint4*>(p.w_readout + col0 + c * 32);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -454,15 +500,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
             }
           }
         }
-        if (lane < nvalid) p.partial[(int64_t)(2 * nt + half) * p.ld_partial + row0 + lane] = dot;
+        if (active && lane < nvalid) p.partial[(int64_t)(2 * nt + part) * p.ld_partial + row0 + lane] = dot;
       } else if constexpr (kEpi == EPI_SWIGLU) {
-        const int col0 = nt * 128 + half * 64;
-        const uint32_t tacc = tmem + lane_off + (uint32_t)buf * 256u + (uint32_t)half * 64u;
+        const int col0 = nt * 128 + part * 64;
+        const uint32_t tacc = tmem + lane_off + (uint32_t)buf * 256u;
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; active && c < 2; ++c) {
           uint32_t g[32], u[32];
-          tmem_ld32(tacc + c * 32, g);
-          tmem_ld32(tacc + 128 + c * 32, u);
+          tmem_ld32(tacc + gcol + c * 32, g);
+          tmem_ld32(tacc + ucol + c * 32, u);
           uint32_t wv[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e)
@@ -471,9 +517,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGsThreads, 1)
           store_rows_coalesced(wv, stage, p.out + row0 * p.ld_out + col0 + c * 32, p.ld_out, nvalid, lane);
         }
       } else {
-        const int hd = 2 * nt + half;
-        if (hd < p.n_heads)
-          qkv_rope_head(p, tmem + lane_off + (uint32_t)buf * 256u + (uint32_t)half * 128u, hd,
+        const int hd = 2 * nt + part;
+        if (active && hd < p.n_heads)
+          qkv_rope_head(p, tmem + lane_off + (uint32_t)buf * 256u + (narrow ? 0u : (uint32_t)half * 128u), hd,
                         smem + Lay::kSmCos + r * Lay::kCsRow, smem + Lay::kSmSin + r * Lay::kCsRow,
                         smem + Lay::kSmGain, stage, p.out + row0 * p.ld_out + (int64_t)hd * 128, nvalid, lane);
         if (rope) {

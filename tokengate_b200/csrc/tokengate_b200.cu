@@ -241,23 +241,38 @@ namespace {
 template <int kEpi>
 int launch_gemm_pair(const void* x, int64_t ld_x, const void* w, int64_t w_rows, int64_t ld_w,
                      tg::GemmPairParams& p, void* stream, const char* name) {
-  CUtensorMap tx, tw;
+  CUtensorMap tx, tw, tw64;
   int st;
   if ((st = encode_2d_bf16(&tx, x, p.M, p.K, ld_x, 128, name))) return st;
   if ((st = encode_2d_bf16(&tw, w, w_rows, p.K, ld_w, 128, name))) return st;
+  if ((st = encode_2d_bf16(&tw64, w, w_rows, p.K, ld_w, 64, name))) return st;  // narrow items' B halves
   p.n_tiles_m = (p.M + 255) / 256;
   const int64_t n_tiles = (int64_t)p.n_tiles_m * p.n_tiles_n;
   if (n_tiles > INT32_MAX) return fail(TG_ERR_UNSUPPORTED, "%s: too many tiles", name);
   p.n_tiles = (int)n_tiles;
+  // Rounds of one tile per CTA pair; when the last round would fill at most
+  // half the pairs, its tiles run as two half-width items each (half the
+  // MMA time per item, the same accumulation order per output).
+  const int64_t pairs = std::max<int64_t>(1, sm_count() / 2);
+  const int64_t full = n_tiles / pairs * pairs, rest = n_tiles - full;
+  int64_t clusters;
+  if (rest > 0 && 2 * rest <= pairs) {
+    p.n_wide = (int)full;
+    p.n_narrow = (int)(2 * rest);
+    clusters = full > 0 ? pairs : 2 * rest;
+  } else {
+    p.n_wide = (int)n_tiles;
+    p.n_narrow = 0;
+    clusters = std::min<int64_t>(n_tiles, pairs);
+  }
   if ((st = device_error_ptr(&p.err))) return st;
   int dev;
   if ((st = current_device(&dev))) return st;
   static bool attr_set[kMaxDevices] = {};
   cudaError_t e = smem_limit_once(tg::gemm_pair_kernel<kEpi>, tg::GemmLayout<kEpi>::kSmemBytes, attr_set, dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_pair smem)");
-  const int64_t clusters = std::max<int64_t>(1, std::min<int64_t>(n_tiles, sm_count() / 2));
   e = launch_pdl(tg::gemm_pair_kernel<kEpi>, dim3((unsigned)(2 * clusters)), dim3(tg::kGsThreads),
-                 (size_t)tg::GemmLayout<kEpi>::kSmemBytes, static_cast<cudaStream_t>(stream), tx, tw, p);
+                 (size_t)tg::GemmLayout<kEpi>::kSmemBytes, static_cast<cudaStream_t>(stream), tx, tw, tw64, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, name);
   return TG_OK;
@@ -832,6 +847,8 @@ int tg_gemm_swiglu(const void* x, int64_t ld_x, const void* w_gu, int64_t ld_w, 
   p.n_tiles_n = inter / 128;
   p.b_step = 128;     // rank 0: W_gate rows 128*nt..; rank 1: the W_up rows inter + 128*nt..
   p.b_rank1 = inter;
+  p.nb_step = 64;     // narrow half j: W_gate rows 128*nt + 64*j.. and the matching W_up rows
+  p.nb_rank1 = inter;
   return launch_gemm_pair<tg::EPI_SWIGLU>(x, ld_x, w_gu, 2 * (int64_t)inter, ld_w, p, stream, "gemm_swiglu");
 }
 
@@ -857,6 +874,8 @@ int tg_gemm_swiglu_readout(const void* x, int64_t ld_x, const void* w_gu, int64_
   p.n_tiles_n = inter / 128;
   p.b_step = 128;  // as gemm_swiglu: rank 0 the W_gate rows, rank 1 the matching W_up rows
   p.b_rank1 = inter;
+  p.nb_step = 64;
+  p.nb_rank1 = inter;
   p.w_readout = static_cast<const __nv_bfloat16*>(w_readout);
   p.partial = partial;
   p.ld_partial = M;
@@ -906,6 +925,8 @@ int tg_gemm_qkv_rope(const void* x, int64_t ld_x, const void* w_qkv, int64_t ld_
   p.n_tiles_n = (n_heads + 1) / 2;   // two heads per column tile
   p.b_step = 256;                     // rank 0: head 2*nt, rank 1: head 2*nt + 1
   p.b_rank1 = 128;
+  p.nb_step = 128;                    // narrow half j: head 2*nt + j, rank 0 its rows 0..63,
+  p.nb_rank1 = 64;                    // rank 1 its rows 64..127
   p.n_q = n_q_heads;
   p.n_k = n_k_heads;
   p.n_heads = n_heads;
