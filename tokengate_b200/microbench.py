@@ -5,6 +5,7 @@
     python -m tokengate_b200.microbench topk   [--k 2000] [--batch 1] [--iters 20]
     python -m tokengate_b200.microbench gather [--k 2000] [--batch 1] [--iters 20]
     python -m tokengate_b200.microbench branch [--seq 32768] [--inter 6144] [--batch 1]
+    python -m tokengate_b200.microbench readout [--seq 32768] [--hidden 2048] [--inter 6144]
     python -m tokengate_b200.microbench tables [--k 2000] [--layers 26] [--hq 16] [--batch 1]
     python -m tokengate_b200.microbench decode [--seq 2768] [--batch 1] [--hq 16] [--hkv 8] [--no-bias]
     python -m tokengate_b200.microbench gemv [--n 12288] [--hidden 2048] [--batch 1]
@@ -240,7 +241,7 @@ def ops_table(dev, tflops_peak: float, hbm_peak_gbs: float, iters: int = 10) -> 
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=("attn", "score", "topk", "gather", "branch", "tables", "decode",
-                                       "generate", "gemv", "gemvchain", "gemm", "qkv"))
+                                       "generate", "gemv", "gemvchain", "gemm", "qkv", "readout"))
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--new", type=int, default=64)
     ap.add_argument("--gate", default="linear", choices=("linear", "e2e"))
@@ -285,6 +286,21 @@ def main(argv=None):
         flops = 2.0 * M * K * 2 * I
         res.update(rows=M, k=K, inter=I, ms=ms, us=ms * 1e3, tflops=flops / ms / 1e9,
                    cublas_us=ms_ref * 1e3, cublas_tflops=flops / ms_ref / 1e9)
+    elif a.kernel == "readout":
+        # the finalized gate's branch as one GEMM (SwiGLU + readout epilogue):
+        # --seq - 768 state rows, --hidden K, --inter; cuBLAS's GEMM + branch_score beside it
+        M, K, I = S - 768, a.hidden, a.inter
+        x = (torch.randn(M, K, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        w = (torch.randn(2 * I, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+        wr = (torch.randn(I, device=dev, generator=g) * I ** -0.5).to(torch.bfloat16)
+        sc = torch.empty(M, device=dev)
+        ms = _graph_time(lambda: ops.gemm_swiglu_readout(x, w, wr, out=sc), 3, a.iters)
+        gu = torch.nn.functional.linear(x, w).unsqueeze(0)
+        ms_ref = _graph_time(lambda: torch.nn.functional.linear(x, w), 3, a.iters)
+        ms_rd = _graph_time(lambda: ops.branch_score(gu, wr, [0], [M]), 3, a.iters)
+        flops = 2.0 * M * K * 2 * I
+        res.update(rows=M, k=K, inter=I, ms=ms, us=ms * 1e3, tflops=flops / ms / 1e9,
+                   cublas_plus_branch_score_us=(ms_ref + ms_rd) * 1e3)
     elif a.kernel == "qkv":
         # the attention input projection with the q/k RMSNorm + RoPE epilogue:
         # --seq rows, --hidden K, --hq / --hkv heads; cuBLAS + qk_norm_rope beside it
