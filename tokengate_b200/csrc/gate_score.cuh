@@ -3,13 +3,12 @@
 // readout plus log-sigmoid; the reference scores with gate(h_art.to(fp32)),
 // tokengate/e2e_gate/gate_module/gate_forward.py:1396-1407).
 //
-// HBM-bound. gate_score_bulk_kernel: one producer warp per CTA streams the
-// CTA's contiguous range of state rows into a ring of shared-memory stages
-// with bulk copies (the TMA engine, one copy per row, completion on an
-// mbarrier per stage), 16 consumer warps (8 for rows over 4 KB) reduce one row each per stage
-// from shared memory with their slice of w in registers. gate_score_kernel
-// (one warp per row, 16-byte non-allocating loads with a one-row prefetch)
-// is kept for rows that are not 16-byte aligned.
+// HBM-bound. gate_score_stream_kernel: one warp per state row over a
+// resident grid (one CTA of 32 warps per SM), each lane loading its 16-byte
+// vectors of the row with non-allocating loads, w staged once per CTA in
+// shared memory. (A bulk-copy form, rows streamed by the TMA engine into a
+// shared-memory ring for consumer warps, measured 35.8 / 227 us for 1 / 8
+// requests against 31.7 / 180 us for this one, and was replaced.)
 // Arithmetic contract (reproducible bit for bit on the host):
 //   lane l accumulates, for i = 0..NV-1 and e = 0..7, the products of the
 //   elements 8*(l + 32*i) + e in that order with fused multiply-adds into one
@@ -34,24 +33,7 @@ struct ScoreParams {
   int64_t total_rows;
   int begin[kScoreMaxReq];
   int64_t row_off[kScoreMaxReq + 1];  // prefix sums of the row counts
-  int64_t rows_per_cta;               // bulk kernel: contiguous rows per CTA
-  unsigned int* err;
 };
-
-constexpr unsigned int ERR_SCORE = 1u << 13;
-// rows per stage (one per consumer warp), stages, threads (consumers + one
-// producer warp) and shared memory of the bulk kernel for NV 16-byte vectors
-// per lane (rows of NV * 512 bytes)
-template <int NV>
-__host__ __device__ constexpr int score_rows() { return NV <= 8 ? 16 : 8; }
-template <int NV>
-__host__ __device__ constexpr int score_stages() { return NV <= 8 ? 3 : 2; }
-template <int NV>
-__host__ __device__ constexpr int score_threads() { return (score_rows<NV>() + 1) * 32; }
-template <int NV>
-__host__ __device__ constexpr int score_bulk_smem() {
-  return score_stages<NV>() * score_rows<NV>() * NV * 512 + 16 * score_stages<NV>() + 128;
-}
 
 // exp(-a) for a >= 0 by Cody-Waite reduction a = k ln2 - r, |r| <= ln2/2, and a
 // degree-7 Taylor polynomial for exp(r); IEEE operations only.
@@ -120,152 +102,46 @@ __device__ __forceinline__ float tg_logsigmoid(float z) {
   return __fsub_rn(fminf(z, 0.0f), l);
 }
 
+// gate_score_stream_kernel: one warp per row over a resident grid (one CTA
+// of 32 warps per SM, 16 for rows over 4 KB), each lane loading its NV
+// 16-byte vectors of the row with non-allocating loads; w is staged once per
+// CTA in shared memory (fp32, read by each lane as the same 8-element slices
+// its vectors cover). The same arithmetic as the kernels above.
 template <int NV>
-__global__ void __launch_bounds__(256) gate_score_kernel(const ScoreParams p) {
+__host__ __device__ constexpr int score_stream_threads() { return NV <= 8 ? 1024 : 512; }
+
+template <int NV>
+__global__ void __launch_bounds__(score_stream_threads<NV>(), 1) gate_score_stream_kernel(const ScoreParams p) {
+  extern __shared__ __align__(16) float s_w[];  // NV * 256 floats
+  for (int i = threadIdx.x; i < NV * 64; i += blockDim.x)
+    reinterpret_cast<float4*>(s_w)[i] = __ldg(reinterpret_cast<const float4*>(p.w) + i);
+  __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int64_t warp_global = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-
-  float wr[NV][8];
+  int req = 0;
+  for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < p.total_rows; g += n_warps) {
+    while (g >= p.row_off[req + 1]) ++req;
+    const __nv_bfloat16* row = p.h + (int64_t)req * p.h_sb + (int64_t)(p.begin[req] + (g - p.row_off[req])) * p.h_ss;
+    uint4 hv[NV];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const float4* wp = reinterpret_cast<const float4*>(p.w + 8 * (lane + 32 * i));
-    const float4 a = __ldg(wp), c = __ldg(wp + 1);
-    wr[i][0] = a.x; wr[i][1] = a.y; wr[i][2] = a.z; wr[i][3] = a.w;
-    wr[i][4] = c.x; wr[i][5] = c.y; wr[i][6] = c.z; wr[i][7] = c.w;
-  }
-
-  // rows are visited in increasing order by each warp; `req` tracks the
-  // request of the row, the next row's 16-byte vectors are loaded before the
-  // current row is reduced
-  int req = 0, nreq = 0;
-  auto row_ptr = [&](int64_t g, int& rq) {
-    while (g >= p.row_off[rq + 1]) ++rq;
-    const int64_t r = g - p.row_off[rq];
-    return p.h + (int64_t)rq * p.h_sb + (int64_t)(p.begin[rq] + r) * p.h_ss;
-  };
-  constexpr bool kPrefetch = NV <= 8;  // wider rows would spill the second buffer
-  uint4 hv[NV], hn[kPrefetch ? NV : 1];
-  int64_t g = warp_global;
-  if (kPrefetch && g < p.total_rows) {
-    const __nv_bfloat16* row = row_ptr(g, nreq);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) hn[i] = ld_nc_v4(reinterpret_cast<const uint4*>(row + 8 * (lane + 32 * i)));
-  }
-  for (; g < p.total_rows; g += n_warps) {
-    if constexpr (kPrefetch) {
-      req = nreq;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) hv[i] = hn[i];
-      const int64_t gn = g + n_warps;
-      if (gn < p.total_rows) {
-        const __nv_bfloat16* row = row_ptr(gn, nreq);
-#pragma unroll
-        for (int i = 0; i < NV; ++i) hn[i] = ld_nc_v4(reinterpret_cast<const uint4*>(row + 8 * (lane + 32 * i)));
-      }
-    } else {
-      const __nv_bfloat16* row = row_ptr(g, req);
-#pragma unroll
-      for (int i = 0; i < NV; ++i) hv[i] = ld_nc_v4(reinterpret_cast<const uint4*>(row + 8 * (lane + 32 * i)));
-    }
+    for (int i = 0; i < NV; ++i) hv[i] = ld_nc_v4(reinterpret_cast<const uint4*>(row + 8 * (lane + 32 * i)));
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv[i]);
+      const float4 wa = reinterpret_cast<const float4*>(s_w)[2 * (lane + 32 * i)];
+      const float4 wb = reinterpret_cast<const float4*>(s_w)[2 * (lane + 32 * i) + 1];
+      const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+      const uint32_t hw[4] = {hv[i].x, hv[i].y, hv[i].z, hv[i].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float lo = __uint_as_float(hw[e] << 16);
-        const float hi = __uint_as_float(hw[e] & 0xFFFF0000u);
-        acc = __fmaf_rn(lo, wr[i][2 * e], acc);
-        acc = __fmaf_rn(hi, wr[i][2 * e + 1], acc);
+        acc = __fmaf_rn(__uint_as_float(hw[e] << 16), wv[2 * e], acc);
+        acc = __fmaf_rn(__uint_as_float(hw[e] & 0xFFFF0000u), wv[2 * e + 1], acc);
       }
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1)
       acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
     if (lane == 0) p.out[(int64_t)req * p.out_sb + (g - p.row_off[req])] = tg_logsigmoid(acc);
-  }
-}
-
-template <int NV>
-__global__ void __launch_bounds__(score_threads<NV>(), 1) gate_score_bulk_kernel(const ScoreParams p) {
-  constexpr int kScoreRowsPerStage = score_rows<NV>();
-  constexpr int ST = score_stages<NV>();
-  constexpr int ROWB = NV * 512;  // bytes of one bf16 row
-  extern __shared__ __align__(128) uint8_t s_smem[];
-  const uint32_t sbase = smem_u32(s_smem);
-  const uint32_t full = sbase + ST * kScoreRowsPerStage * ROWB;
-  const uint32_t empty = full + 8 * ST;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int k = 0; k < ST; ++k) {
-      mbar_init(full + 8u * k, 1);
-      mbar_init(empty + 8u * k, kScoreRowsPerStage);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-  const int64_t g0 = (int64_t)blockIdx.x * p.rows_per_cta;
-  const int64_t g1 = g0 + p.rows_per_cta < p.total_rows ? g0 + p.rows_per_cta : p.total_rows;
-  const int n_it = (int)((g1 - g0 + kScoreRowsPerStage - 1) / kScoreRowsPerStage);
-
-  if (warp == kScoreRowsPerStage) {
-    // ---------------------------------------------------------------- producer
-    if (lane == 0) {
-      int rq = 0;
-      for (int it = 0; it < n_it; ++it) {
-        const int k = it % ST;
-        if (it >= ST && !mbar_wait(empty + 8u * k, (uint32_t)((it / ST) - 1) & 1u, p.err, ERR_SCORE)) break;
-        const int64_t gb = g0 + (int64_t)it * kScoreRowsPerStage;
-        const int nr = (int)(g1 - gb < kScoreRowsPerStage ? g1 - gb : kScoreRowsPerStage);
-        mbar_arrive_expect_tx(full + 8u * k, (uint32_t)(nr * ROWB));
-        for (int w = 0; w < nr; ++w) {
-          const int64_t g = gb + w;
-          while (g >= p.row_off[rq + 1]) ++rq;
-          const __nv_bfloat16* row = p.h + (int64_t)rq * p.h_sb + (p.begin[rq] + (g - p.row_off[rq])) * p.h_ss;
-          bulk_load(sbase + (uint32_t)((k * kScoreRowsPerStage + w) * ROWB), row, ROWB, full + 8u * k);
-        }
-      }
-    }
-    return;
-  }
-  // ------------------------------------------------------------------ consumers
-  float wr[NV][8];
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const float4* wp = reinterpret_cast<const float4*>(p.w + 8 * (lane + 32 * i));
-    const float4 a = __ldg(wp), c = __ldg(wp + 1);
-    wr[i][0] = a.x; wr[i][1] = a.y; wr[i][2] = a.z; wr[i][3] = a.w;
-    wr[i][4] = c.x; wr[i][5] = c.y; wr[i][6] = c.z; wr[i][7] = c.w;
-  }
-  int rq = 0;
-  for (int it = 0; it < n_it; ++it) {
-    const int k = it % ST;
-    if (!__all_sync(0xffffffffu, mbar_wait(full + 8u * k, (uint32_t)(it / ST) & 1u, p.err, ERR_SCORE))) break;
-    const int64_t g = g0 + (int64_t)it * kScoreRowsPerStage + warp;
-    if (g < g1) {
-      const uint8_t* rowp = s_smem + (k * kScoreRowsPerStage + warp) * ROWB;
-      float acc = 0.f;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const uint4 v = *reinterpret_cast<const uint4*>(rowp + 16 * (lane + 32 * i));
-        const uint32_t hw[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float lo = __uint_as_float(hw[e] << 16);
-          const float hi = __uint_as_float(hw[e] & 0xFFFF0000u);
-          acc = __fmaf_rn(lo, wr[i][2 * e], acc);
-          acc = __fmaf_rn(hi, wr[i][2 * e + 1], acc);
-        }
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1)
-        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
-      while (g >= p.row_off[rq + 1]) ++rq;
-      if (lane == 0) p.out[(int64_t)rq * p.out_sb + (g - p.row_off[rq])] = tg_logsigmoid(acc);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty + 8u * k);
   }
 }
 

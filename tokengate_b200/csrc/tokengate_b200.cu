@@ -506,21 +506,20 @@ int tg_gate_score(const void* hidden, int64_t h_sb, int64_t h_ss, int hidden_dim
     }
     p.total_rows = p.row_off[nb];
     if (p.total_rows == 0) continue;
-    // one CTA per SM, each streaming a contiguous range of rows
+    // one CTA of one warp per row at a time per SM, rows grid-strided
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess)
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int st;
-    if ((st = device_error_ptr(&p.err))) return st;
     void (*kern)(const tg::ScoreParams) = nullptr;
-    int smem = 0;
+    int smem = 0, threads = 0;
     cudaError_t e = cudaSuccess;
     switch (nv) {
 #define TG_SCORE_CASE(NV)                                                              \
       case NV: {                                                                       \
         static bool attr_set[kMaxDevices] = {};                                        \
-        kern = tg::gate_score_bulk_kernel<NV>;                                         \
-        smem = tg::score_bulk_smem<NV>();                                              \
+        kern = tg::gate_score_stream_kernel<NV>;                                       \
+        smem = NV * 256 * (int)sizeof(float);                                          \
+        threads = tg::score_stream_threads<NV>();                                      \
         e = smem_limit_once(kern, smem, attr_set, dev);                                \
         break;                                                                         \
       }
@@ -534,11 +533,9 @@ int tg_gate_score(const void* hidden, int64_t h_sb, int64_t h_ss, int hidden_dim
 #undef TG_SCORE_CASE
     }
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gate score smem)");
-    const int rows = nv <= 8 ? 16 : 8, threads = (rows + 1) * 32;  // score_rows / score_threads
-    int64_t rpc = (p.total_rows + sms - 1) / sms;
-    rpc = (rpc + rows - 1) / rows * rows;
-    p.rows_per_cta = rpc;
-    const int64_t blocks = (p.total_rows + rpc - 1) / rpc;
+    const int64_t warps_per_cta = threads / 32;
+    const int64_t want = (p.total_rows + warps_per_cta - 1) / warps_per_cta;
+    const int64_t blocks = want < sms ? want : sms;
     kern<<<(unsigned)blocks, threads, smem, s>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gate score launch");
