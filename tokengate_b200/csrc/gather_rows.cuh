@@ -4,8 +4,8 @@
 // (tokengate/e2e_gate/gate_module/gate_forward.py:1443-1461, :1491-1522).
 //
 // HBM-bound copy: one warp per (request, tensor, row); lanes move 16-byte
-// vectors with non-allocating loads, four in flight per lane before the
-// stores. Rows at or past the request's n_valid are zero-filled, as the
+// vectors with non-allocating loads, eight in flight per lane before the
+// stores for single-segment rows (four for segmented ones). Rows at or past the request's n_valid are zero-filled, as the
 // reference's zero-initialised / F.pad-ed outputs are.
 #pragma once
 
@@ -46,6 +46,28 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherParams p) 
     const int seg_vecs = (int)(T.seg_bytes >> 4);
     const int n_vec = seg_vecs * T.n_seg;
     int v = lane;
+    if (T.n_seg == 1) {
+      // one contiguous segment (token-major tensors): eight vectors in flight
+      // per lane, no segment arithmetic
+      const uint4* s4 = reinterpret_cast<const uint4*>(src);
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+      for (; v + 224 < n_vec; v += 256) {
+        uint4 x[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) x[u] = valid ? ld_nc_v4(s4 + v + 32 * u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) d4[v + 32 * u] = x[u];
+      }
+      for (; v + 96 < n_vec; v += 128) {
+        uint4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = valid ? ld_nc_v4(s4 + v + 32 * u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) d4[v + 32 * u] = x[u];
+      }
+      for (; v < n_vec; v += 32) d4[v] = valid ? ld_nc_v4(s4 + v) : make_uint4(0, 0, 0, 0);
+      continue;
+    }
     for (; v + 96 < n_vec; v += 128) {
       uint4 x[4];
 #pragma unroll
