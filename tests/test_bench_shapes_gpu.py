@@ -9,9 +9,10 @@
   * Phase-2 attention: S=2768 (512 prefix + K=2000 + 256 suffix), the bench's
     per-key bias row (bf16 values, -1e9 pads on a shorter second request),
     and the finalized gate's form: a per-head bias with a per-row query scale;
-  * top-K on the global-memory path (more than 32768 state scores): 130304
-    bf16-rounded scores with ties at the K=4000 boundary, and a batch that
-    mixes it with a 32000-score request and a tiny one, bit-exact against both
+  * top-K past 32768 state scores (a cluster of CTAs per request, the
+    global-memory kernel past 8 x 32768): 130304 bf16-rounded scores with ties
+    at the K=4000 boundary, the cluster sizes' edges, and a batch that mixes it
+    with a 32000-score request and a tiny one, bit-exact against both
     selection oracles;
   * attention at the long-context shape: S=131072, 32 query / 8 KV heads;
   * the whole gated prefill of the Qwen3-1.7B-shape model at 8192 tokens,
@@ -137,9 +138,19 @@ def test_topk_global_path_130k_ties(cuda):
     _check_topk([s], [4000], [512], [131072], 512 + 4000 + 256, cuda)
 
 
+@pytest.mark.parametrize("n,K", [(32769, 32768), (70000, 3000), (130304, 1), (262144, 4000), (262145, 4000)])
+def test_topk_cluster_and_global_sizes(cuda, n, K):
+    """Past 32768 scores one request runs on a cluster of CTAs (2, 3, 4 and the
+    maximum 8 here: 32769 leaves one score to the second CTA), past 8 x 32768
+    on the global-memory kernel; bf16 ties at the K-th value."""
+    s = _bf16_scores(n, n + K)
+    _check_topk([s], [K], [512], [n + 768], 512 + K + 256, cuda)
+
+
 def test_topk_global_path_mixed_batch(cuda):
     """One launch over requests of 130304, 32000 and 5 state scores (the batch
-    takes the global-memory kernel), K = 4000 / 2000 / 2 and all-tied rows."""
+    takes the CTA-cluster kernel: the two short requests leave three of their
+    four CTAs without scores), K = 4000 / 2000 / 2 and all-tied rows."""
     a = _bf16_scores(130304, 1)
     b = _bf16_scores(32000, 2)
     c = np.full(5, -0.5, dtype=np.float32)

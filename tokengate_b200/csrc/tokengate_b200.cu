@@ -593,7 +593,24 @@ int tg_topk_select(const float* scores, int64_t s_sb, int B, const int32_t* n_st
       tg::topk_select_reg_kernel<8><<<nb, tg::kTopkThreads, 0, s>>>(p);
     else if (n_max <= tg::kTopkThreads * tg::kTopkRegKeys)
       tg::topk_select_reg_kernel<tg::kTopkRegKeys><<<nb, tg::kTopkThreads, 0, s>>>(p);
-    else
+    else if (n_max <= tg::kTopkMaxCluster * tg::kTopkThreads * tg::kTopkRegKeys) {
+      // a cluster of CTAs per request, each holding 32768 scores in registers
+      const int per = tg::kTopkThreads * tg::kTopkRegKeys;
+      const unsigned C = (unsigned)((n_max + per - 1) / per);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(C, (unsigned)nb);
+      cfg.blockDim = dim3(tg::kTopkThreads);
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = C;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cudaError_t el = cudaLaunchKernelEx(&cfg, tg::topk_select_cluster_kernel, p);
+      if (el != cudaSuccess) return cuda_fail(el, "top-k cluster launch");
+    } else
       tg::topk_select_kernel<<<nb, tg::kTopkThreads, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "top-k launch");

@@ -332,4 +332,150 @@ __global__ void __launch_bounds__(kTopkThreads, 1) topk_select_reg_kernel(const 
   topk_write_fixed(p, b, begin, K, end, n_kept, keep);
 }
 
+// Requests with kTopkThreads * kTopkRegKeys < n_state <= kTopkMaxCluster
+// times that: a cluster of C = gridDim.x CTAs per request (grid (C, requests)).
+// CTA r holds the scores [32768 r, 32768 (r + 1)) in registers as
+// topk_select_reg_kernel holds its own. Each digit pass's histogram is the sum
+// of the CTAs' shared-memory histograms, read through distributed shared
+// memory in rank order, so every CTA takes the same decision; in the
+// compaction, CTA r's offsets add the T-equal and selected counts of CTAs
+// 0..r-1, keeping the index order of the whole request. Same results as the
+// single-CTA kernels. Every CTA runs the same cluster barriers (none returns
+// early), so each barrier completes.
+constexpr int kTopkMaxCluster = 8;
+__global__ void __launch_bounds__(kTopkThreads, 1) topk_select_cluster_kernel(const TopkParams p) {
+  constexpr int KPT = kTopkRegKeys;
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_warp[32];
+  __shared__ uint32_t s_bin, s_need, s_total;
+  __shared__ uint32_t s_cnt[2];  // this CTA's T-equal and above-T key counts
+  __shared__ uint32_t s_off[2];  // T-equal and selected keys of the lower-rank CTAs
+
+  const int C = (int)gridDim.x;
+  const uint32_t rank_c = cluster_ctarank();
+  const int b = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = p.n_state[b];
+  const int K = p.k[b];
+  const int begin = p.begin[b];
+  const int end = begin + n;
+  const int n_kept = begin + K + (p.seq_len[b] - end);
+  const float* sc = p.scores + (int64_t)b * p.s_sb;
+  const int i0 = (int)rank_c * (kTopkThreads * KPT) + tid * KPT;
+
+  uint32_t key[KPT];
+  const bool vec = ((reinterpret_cast<uintptr_t>(sc) & 15) == 0) && (i0 + KPT <= n);
+  if (vec) {
+#pragma unroll
+    for (int e = 0; e < KPT; e += 4) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(sc + i0 + e));
+      key[e] = order_key(f.x); key[e + 1] = order_key(f.y);
+      key[e + 2] = order_key(f.z); key[e + 3] = order_key(f.w);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < KPT; ++e) key[e] = order_key((i0 + e < n) ? __ldg(sc + i0 + e) : 0.f);
+  }
+  const int n_mine = max(0, min(KPT, n - i0));
+
+  uint32_t prefix = 0, mask = 0, need = (uint32_t)K;
+#pragma unroll 1
+  for (int d = 3; d >= 0; --d) {
+    const int shift = 8 * d;
+    if (tid < 256) hist[tid] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < KPT; ++e) {
+      const uint32_t digit = (e < n_mine && (key[e] & mask) == prefix) ? (key[e] >> shift) & 255u : 256u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+      if (digit < 256 && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+    }
+    cluster_sync_all();  // every CTA's histogram of this pass is complete
+    if (warp == 0) {
+      uint32_t c[8], sum = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t a = smem_u32(&hist[255 - (lane * 8 + e)]);
+        uint32_t v = 0;
+        for (int q = 0; q < C; ++q) v += ld_shared_cluster_u32(mapa_shared(a, (uint32_t)q));
+        c[e] = v;
+        sum += v;
+      }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      const uint32_t excl = incl - sum;
+      if (excl < need && need <= incl) {
+        uint32_t run = excl;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (run + c[e] >= need) {
+            s_bin = 255 - (lane * 8 + e);
+            s_need = need - run;
+            break;
+          }
+          run += c[e];
+        }
+      }
+    }
+    cluster_sync_all();  // the remote reads are done before any CTA clears its histogram
+    prefix |= s_bin << shift;
+    mask |= 255u << shift;
+    need = s_need;
+  }
+  const uint32_t T = prefix;
+
+  uint32_t n_gt = 0, n_eq = 0;
+#pragma unroll
+  for (int e = 0; e < KPT; ++e) {
+    n_gt += (e < n_mine && key[e] > T);
+    n_eq += (e < n_mine && key[e] == T);
+  }
+  const uint32_t eq_local = block_excl_scan(n_eq, s_warp, &s_total);
+  if (tid == 0) s_cnt[0] = s_total;
+  (void)block_excl_scan(n_gt, s_warp, &s_total);
+  if (tid == 0) s_cnt[1] = s_total;
+  cluster_sync_all();  // every CTA's counts are published
+  if (tid == 0) {
+    uint32_t eq_b = 0, sel_b = 0;
+    for (int q = 0; q < (int)rank_c; ++q) {
+      const uint32_t E = ld_shared_cluster_u32(mapa_shared(smem_u32(&s_cnt[0]), (uint32_t)q));
+      const uint32_t G = ld_shared_cluster_u32(mapa_shared(smem_u32(&s_cnt[1]), (uint32_t)q));
+      const uint32_t take = need > eq_b ? min(E, need - eq_b) : 0u;
+      sel_b += G + take;
+      eq_b += E;
+    }
+    s_off[0] = eq_b;
+    s_off[1] = sel_b;
+  }
+  cluster_sync_all();  // no CTA leaves while another still reads its counts
+  const uint32_t eq_before = s_off[0] + eq_local;
+  const uint32_t take_eq = (need > eq_before) ? min(n_eq, need - eq_before) : 0u;
+  const uint32_t out_before = s_off[1] + block_excl_scan(n_gt + take_eq, s_warp, &s_total);
+
+  int64_t* keep = p.keep + (int64_t)b * p.keep_sb;
+  int64_t* tl = p.topk_local ? p.topk_local + (int64_t)b * p.tl_sb : nullptr;
+  uint32_t rank = out_before, eq_seen = 0;
+#pragma unroll
+  for (int e = 0; e < KPT; ++e) {
+    if (e < n_mine) {
+      bool sel = key[e] > T;
+      if (key[e] == T) {
+        sel = eq_seen < take_eq;
+        ++eq_seen;
+      }
+      if (sel) {
+        keep[begin + rank] = begin + i0 + e;
+        if (tl) tl[rank] = i0 + e;
+        store_bias(p, b, begin + (int)rank, key_value(key[e]));
+        ++rank;
+      }
+    }
+  }
+  if (rank_c == 0) topk_write_fixed(p, b, begin, K, end, n_kept, keep);
+}
+
 }  // namespace tg
