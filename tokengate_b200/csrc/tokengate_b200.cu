@@ -589,13 +589,9 @@ int tg_topk_select(const float* scores, int64_t s_sb, int B, const int32_t* n_st
     }
     int n_max = 0;
     for (int i = 0; i < nb; ++i) n_max = p.n_state[i] > n_max ? p.n_state[i] : n_max;
-    if (n_max <= tg::kTopkThreads * 8)
-      tg::topk_select_reg_kernel<8><<<nb, tg::kTopkThreads, 0, s>>>(p);
-    else if (n_max <= tg::kTopkThreads * tg::kTopkRegKeys)
-      tg::topk_select_reg_kernel<tg::kTopkRegKeys><<<nb, tg::kTopkThreads, 0, s>>>(p);
-    else if (n_max <= tg::kTopkMaxCluster * tg::kTopkThreads * tg::kTopkRegKeys) {
-      // a cluster of CTAs per request, each holding 32768 scores in registers
-      const int per = tg::kTopkThreads * tg::kTopkRegKeys;
+    // a cluster of CTAs per request, each holding 1024 * kpt scores in registers
+    auto launch_cluster = [&](auto kern, int kpt) {
+      const int per = tg::kTopkThreads * kpt;
       const unsigned C = (unsigned)((n_max + per - 1) / per);
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(C, (unsigned)nb);
@@ -608,10 +604,18 @@ int tg_topk_select(const float* scores, int64_t s_sb, int B, const int32_t* n_st
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      cudaError_t el = cudaLaunchKernelEx(&cfg, tg::topk_select_cluster_kernel, p);
-      if (el != cudaSuccess) return cuda_fail(el, "top-k cluster launch");
-    } else
+      return cudaLaunchKernelEx(&cfg, kern, p);
+    };
+    cudaError_t el = cudaSuccess;
+    if (n_max <= tg::kTopkThreads * 8)
+      tg::topk_select_reg_kernel<8><<<nb, tg::kTopkThreads, 0, s>>>(p);
+    else if (n_max <= tg::kTopkThreads * tg::kTopkRegKeys)
+      el = launch_cluster(tg::topk_select_cluster_kernel<8>, 8);  // 2-4 CTAs of 8192 scores
+    else if (n_max <= tg::kTopkMaxCluster * tg::kTopkThreads * tg::kTopkRegKeys)
+      el = launch_cluster(tg::topk_select_cluster_kernel<tg::kTopkRegKeys>, tg::kTopkRegKeys);
+    else
       tg::topk_select_kernel<<<nb, tg::kTopkThreads, 0, s>>>(p);
+    if (el != cudaSuccess) return cuda_fail(el, "top-k cluster launch");
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "top-k launch");
   }

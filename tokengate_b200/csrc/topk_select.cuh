@@ -1,5 +1,7 @@
-// Top-K selection of state tokens and the kept-position list — one CTA per
-// request, single pass radix select.
+// Top-K selection of state tokens and the kept-position list — radix select
+// with the scores in registers: one CTA per request up to 8192 scores, a
+// cluster of CTAs per request beyond (topk_select_cluster_kernel), the
+// global-memory kernel past 8 x 32768.
 //
 // Reference semantics (tokengate/e2e_gate/gate_module/gate_forward.py):
 //   topk = torch.topk(score, K_clamped).indices                   :84-99
@@ -332,9 +334,10 @@ __global__ void __launch_bounds__(kTopkThreads, 1) topk_select_reg_kernel(const 
   topk_write_fixed(p, b, begin, K, end, n_kept, keep);
 }
 
-// Requests with kTopkThreads * kTopkRegKeys < n_state <= kTopkMaxCluster
-// times that: a cluster of C = gridDim.x CTAs per request (grid (C, requests)).
-// CTA r holds the scores [32768 r, 32768 (r + 1)) in registers as
+// A cluster of C = gridDim.x CTAs per request (grid (C, requests)), for
+// requests past one CTA's registers (KPT = 32: up to kTopkMaxCluster x 32768
+// scores) or to spread a 32 k request over four CTAs (KPT = 8). CTA r holds
+// the scores [1024 KPT r, 1024 KPT (r + 1)) in registers as
 // topk_select_reg_kernel holds its own. Each digit pass's histogram is the sum
 // of the CTAs' shared-memory histograms, read through distributed shared
 // memory in rank order, so every CTA takes the same decision; in the
@@ -343,8 +346,8 @@ __global__ void __launch_bounds__(kTopkThreads, 1) topk_select_reg_kernel(const 
 // single-CTA kernels. Every CTA runs the same cluster barriers (none returns
 // early), so each barrier completes.
 constexpr int kTopkMaxCluster = 8;
+template <int KPT>
 __global__ void __launch_bounds__(kTopkThreads, 1) topk_select_cluster_kernel(const TopkParams p) {
-  constexpr int KPT = kTopkRegKeys;
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s_warp[32];
   __shared__ uint32_t s_bin, s_need, s_total;
