@@ -284,10 +284,9 @@ int launch_gemm_pair(const void* x, int64_t ld_x, const void* w, int64_t w_rows,
 // SM, and a CTA costs kFix + key blocks * (kPair for two heads, kSingle for
 // one), in microseconds: kFix and kPair from a global-timer trace of the
 // S=2768 launch, kSingle fitted to launches with 0..8 single-head rows
-// (S=2768: 51, 51, 49, 47, 48, 51, 55, 62 us; S=4096: 0 rows fastest). The
-// smallest count within 0.5 % of the shortest modelled span wins; launches
-// of more than two waves of head pairs keep 0 (their tail is a small share).
-// Memoised per shape.
+// (S=2768: 51, 51, 49, 47, 48, 51, 55, 62 us; S=4096: 0 rows fastest).
+// Launches of more than two waves of head pairs keep 0 (their tail is a
+// small share). Memoised per shape.
 int attn_single_rows(int n_mblocks, int Hq, int B, int sms) {
   constexpr double kFix = 5.3, kPair = 2.0, kSingle = 1.8;
   const int64_t pair_ctas = (int64_t)n_mblocks * (Hq / 2) * B;
@@ -318,15 +317,25 @@ int attn_single_rows(int n_mblocks, int Hq, int B, int sms) {
     }
     return end;
   };
-  int best_t = 0;
-  double best = span(0);
-  for (int T = 1; T < n_mblocks && T <= 64; ++T) {
-    const double sp = span(T);
-    if (sp < best * 0.995) {
-      best = sp;
-      best_t = T;
-    }
+  const int t_max = n_mblocks - 1 < 64 ? n_mblocks - 1 : 64;
+  std::vector<double> sp(t_max + 1);
+  double best = 1e300;
+  for (int T = 0; T <= t_max; ++T) {
+    sp[T] = span(T);
+    best = sp[T] < best ? sp[T] : best;
   }
+  // Among the counts within 0.5 % of the shortest span: the largest whose
+  // CTAs still fit in one wave (idle SMs make the extra CTAs free; measured
+  // at 868 and 1268 keys: 174 / 283 TFLOP/s with 1 row, 184-188 / 297-298
+  // with 3-8), else the smallest.
+  int best_t = -1;
+  for (int T = 0; T <= t_max; ++T) {
+    const int64_t ctas = (int64_t)B * ((int64_t)(n_mblocks - T) * (Hq / 2) + (int64_t)T * Hq);
+    if (sp[T] <= best * 1.005 && ctas <= sms) best_t = T;
+  }
+  if (best_t < 0)
+    for (int T = 0; T <= t_max && best_t < 0; ++T)
+      if (sp[T] <= best * 1.005) best_t = T;
   std::lock_guard<std::mutex> lk(mu);
   memo[key] = best_t;
   return best_t;
