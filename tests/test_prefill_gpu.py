@@ -222,3 +222,29 @@ def test_load_model_synthetic(cuda):
     assert out.n_kept == [3 + 16 + 2]
     with pytest.raises(ValueError):
         load_model(base_model=small, gate_layer=1, gate_attn="flex", device=cuda)
+
+
+def test_phase2_rotary_rows_gathered_from_phase1_table(cuda):
+    """The fused prefill's Phase-2 cos / sin: rows of Phase 1's table of
+    positions 0..S-1 gathered at the kept positions (pad slots at position 0)
+    equal the rotary module evaluated at those positions, bit for bit."""
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+    cfg = Qwen3Config(hidden_size=2048, num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                      rope_theta=1e6, max_position_embeddings=40960)
+    rot = Qwen3RotaryEmbedding(cfg).to(cuda)
+    S, n_alloc = 32768, 2768
+    h = torch.zeros(2, S, 8, dtype=torch.bfloat16, device=cuda)
+    cos_t, sin_t = tgp._phase1_rope(rot, h, S, 2)
+    g = torch.Generator().manual_seed(0)
+    kept = torch.zeros(2, n_alloc, dtype=torch.int64)
+    kept[0, :2700] = torch.sort(torch.randperm(S, generator=g)[:2700]).values
+    kept[1] = torch.sort(torch.randperm(S, generator=g)[:n_alloc]).values
+    kept = kept.to(cuda)
+    cos2 = torch.empty(2, n_alloc, 128, dtype=torch.bfloat16, device=cuda)
+    sin2 = torch.empty_like(cos2)
+    ops.gather_rows([ops.gather_spec_rows(cos_t, cos2, 1), ops.gather_spec_rows(sin_t, sin2, 1)],
+                    kept, [n_alloc, n_alloc], n_alloc, cuda)
+    ref_cos, ref_sin = rot(h[:, :n_alloc], kept)
+    torch.cuda.synchronize()
+    assert torch.equal(cos2, ref_cos) and torch.equal(sin2, ref_sin)

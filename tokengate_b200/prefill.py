@@ -209,7 +209,7 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
     x2 = None
     pe = None
     if fused:
-        cos, sin = _phase1_rope(inner.rotary_emb, hidden, max_seq_len, B)
+        cos, sin = rope1 = _phase1_rope(inner.rotary_emb, hidden, max_seq_len, B)
         delta = None
         for i in range(gate_layer if e2e else gate_layer + 1):
             hidden, delta = layer_forward(fw[i], hidden, delta, cos, sin, cache, i)
@@ -275,7 +275,19 @@ def prefill_batch_for_decode(model: torch.nn.Module, gate, prompt_ids_list: Sequ
     del hidden, scores
 
     # ---- Phase 2
-    pe2 = inner.rotary_emb(hs_pruned, kept_positions)
+    if fused:
+        # the kept positions' rotary rows, gathered from Phase 1's table of
+        # positions 0..S-1 (the same values the rotary module gives them; pad
+        # slots hold position 0, so every row is gathered)
+        D = rope1[0].shape[-1]
+        cos2 = torch.empty((B, n_alloc, D), dtype=rope1[0].dtype, device=device)
+        sin2 = torch.empty_like(cos2)
+        ops.gather_rows([ops.gather_spec_rows(rope1[0], cos2, 1), ops.gather_spec_rows(rope1[1], sin2, 1)],
+                        kept_positions, [n_alloc] * B, n_alloc, device)
+        pe2 = (cos2, sin2)
+        del rope1
+    else:
+        pe2 = inner.rotary_emb(hs_pruned, kept_positions)
     # pinned source, asynchronous copy: a pageable one would synchronise the stream
     last_valid = torch.tensor([n - 1 for n in n_kepts], dtype=torch.long,
                               pin_memory=torch.cuda.is_available()).to(device, non_blocking=True)
