@@ -13,7 +13,8 @@
     python -m tokengate_b200.microbench generate [--seq 32768] [--k 2000] [--batch 1] [--new 64] [--gate linear|e2e] [--proj gemv|cublas]
 
 Prints one JSON line per run with the CUDA-event time per launch and the
-algorithmic FLOPs or bytes of one launch (attention: 4*B*Hq*D*S(S+1)/2;
+algorithmic FLOPs or bytes of one launch (attention: 4*B*Hq*D*S(S+1)/2, also
+timed as 10 launches in one CUDA graph, `ms_graph`;
 score: the bf16 state rows + w + fp32 scores; topk: scores read + keep/bias
 written; gather: hidden rows + 4 below-gate K/V tensors read and written;
 branch: the bf16 [gate | up] state rows + w + fp32 scores; tables: the raw
@@ -380,10 +381,15 @@ def main(argv=None):
         k = torch.randn(B, S, a.hkv, 128, device=dev, dtype=torch.bfloat16, generator=g)
         v = torch.randn(B, S, a.hkv, 128, device=dev, dtype=torch.bfloat16, generator=g)
         bias = None if a.no_bias else torch.randn(B, 1, S, device=dev, generator=g)
-        ms = _time(lambda: ops.keybias_attention(q, k, v, bias=bias), a.iters)
+        o = torch.empty_like(q)
+        ms = _time(lambda: ops.keybias_attention(q, k, v, bias=bias, out=o), a.iters)
+        # 10 launches in one CUDA graph, as the Phase-2 layers replay them: the
+        # host's launch path is not timed and consecutive launches overlap
+        # their prologues (programmatic stream serialization)
+        ms_graph = _graph_time(lambda: ops.keybias_attention(q, k, v, bias=bias, out=o), 10, a.iters)
         flops = 4.0 * B * a.hq * 128 * S * (S + 1) / 2
         res.update(seq=S, hq=a.hq, hkv=a.hkv, bias=not a.no_bias, ms=ms, tflop=flops / 1e12,
-                   tflops=flops / ms / 1e9)
+                   tflops=flops / ms / 1e9, ms_graph=ms_graph, tflops_graph=flops / ms_graph / 1e9)
     elif a.kernel == "branch":
         n_art = S - 768
         gu = torch.randn(B, n_art, 2 * a.inter, device=dev, dtype=torch.bfloat16, generator=g)
